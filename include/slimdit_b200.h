@@ -1,0 +1,112 @@
+/*
+ * slimdit_b200 — C ABI of the B200 (sm_100a) convrot W8A8 linear and weight converter.
+ *
+ * Conventions for every entry point:
+ *   - All array arguments are device pointers owned by the caller; shapes are element
+ *     counts; matrices are row-major. `stream` is a cudaStream_t passed as void* (NULL =
+ *     legacy default stream). Calls are stream-ordered and do not synchronise.
+ *   - Return 0 on success or a negative SLIM_ERR_* code; no exception crosses the ABI.
+ *     slim_last_error() returns the message of the calling thread's last failure.
+ *   - Device pointers must be 16-byte aligned; rows are contiguous (pitch = K).
+ *   - Kernel-side waits are bounded; slim_device_error() reports (and clears) a wait that
+ *     ran out.
+ *
+ * Rotation orders (`order`):
+ *   SLIM_ORDER_REFERENCE reproduces the reference's fp32 summation order of
+ *     `np.matmul(grouped, H.T)` (slimdit/hadamard.py:56-58, numpy 2.3 + OpenBLAS 0.3.30
+ *     on x86-64), so codes and scales equal slimdit.int8.quantize_convrot_weight's bit for
+ *     bit. Compute-bound (~256 fp32 FMAs per element).
+ *   SLIM_ORDER_BUTTERFLY is the radix-4 fast Hadamard transform (memory-bound), used for
+ *     activations.
+ */
+#ifndef SLIMDIT_B200_H_
+#define SLIMDIT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SLIM_ABI_VERSION 1
+
+enum slim_status {
+  SLIM_OK = 0,
+  SLIM_ERR_SHAPE = -1,       /* bad or unsupported shape */
+  SLIM_ERR_ALIGN = -2,       /* pointer or pitch not 16-byte aligned */
+  SLIM_ERR_GROUP = -3,       /* group size other than 256, or K % 256 != 0 */
+  SLIM_ERR_ARCH = -4,        /* device is not sm_100 */
+  SLIM_ERR_CUDA = -5,        /* CUDA runtime error (see slim_last_error) */
+  SLIM_ERR_DTYPE = -6,       /* unsupported dtype / order / epilogue code */
+  SLIM_ERR_NULL = -7         /* required pointer is NULL */
+};
+
+enum slim_dtype { SLIM_F32 = 0, SLIM_BF16 = 1, SLIM_F16 = 2 };
+enum slim_order { SLIM_ORDER_REFERENCE = 0, SLIM_ORDER_BUTTERFLY = 1 };
+enum slim_epilogue { SLIM_EPI_SCALE_BIAS = 0, SLIM_EPI_GELU_TANH = 1 };
+
+/* ABI version (SLIM_ABI_VERSION). */
+int slim_version(void);
+
+/* Copies the calling thread's last error message (NUL-terminated) into buf.
+ * Returns the message length. */
+int slim_last_error(char* buf, size_t len);
+
+/* Synchronises the current device, stores the device error word (0 = none; see
+ * slim_ptx.cuh DeviceError) in *code and clears it. */
+int slim_device_error(unsigned int* code);
+
+/* Number of kernels this library has launched since it was loaded. */
+uint64_t slim_launch_count(void);
+
+/* Group-wise rotation out = W @ H^T over groups of 256 input features, fp32 result.
+ * Replaces slimdit.hadamard.rotate(weight, h, group_size) (slimdit/hadamard.py:45-58).
+ * x: [rows, K] of `dtype`; out: fp32 [rows, K]. */
+int slim_rotate_f32(const void* x, int dtype, int64_t rows, int64_t K, int group, int order,
+                    float* out, void* stream);
+
+/* Rotation fused with per-row symmetric INT8 quantisation:
+ *   scale[r] = max(absmax_r / 127, 1e-30),  q = clip(rint(rot / scale), -128, 127).
+ * Replaces slimdit.int8.quantize_convrot_weight (slimdit/int8.py:39-52) for weights
+ * (order REFERENCE) and the per-token activation quantisation inside the runtime's
+ * int8_linear (tools/bench_int8.py:65-68) (order BUTTERFLY).
+ * q: int8 [rows, K]; scale: fp32 [rows]; rot_out: optional fp32 [rows, K] copy of the
+ * rotated values (NULL to skip). BUTTERFLY requires K <= 16384. */
+int slim_rotate_quant_i8(const void* x, int dtype, int64_t rows, int64_t K, int group,
+                         int order, int8_t* q, float* scale, float* rot_out, void* stream);
+
+/* Quantisation stage alone on already-rotated fp32 rows (slimdit/int8.py:49-51). */
+int slim_quantize_rows_i8(const float* rotated, int64_t rows, int64_t K, int8_t* q,
+                          float* scale, void* stream);
+
+/* out = (q * scale) @ H^T in the reference order.
+ * Replaces slimdit.int8.dequantize_convrot_weight (slimdit/int8.py:55-61). */
+int slim_dequant_i8(const int8_t* q, const float* scale, int64_t rows, int64_t K, int group,
+                    float* out, void* stream);
+
+/* out[m,n] = bf16(float(sum_k a[m,k]*b[n,k]) * (sa[m]*sb[n]) + bias[n]), optionally
+ * followed by GELU-tanh (SLIM_EPI_GELU_TANH: applied to the bf16-rounded linear output,
+ * result rounded to bf16). a: int8 [M,K]; b: int8 [N,K]; sa: fp32 [M]; sb: fp32 [N];
+ * bias: bf16 [N] or NULL; out: bf16 [M,N]; acc_dbg: int32 [M,N] or NULL (raw
+ * accumulators). Requires K % 16 == 0 and N % 8 == 0.
+ * The int8 GEMM + dequant inside the runtime's int8_linear (tools/bench_int8.py:65-68;
+ * math at slimdit/int8.py:9-11). */
+int slim_gemm_i8(const int8_t* a, const int8_t* b, const float* sa, const float* sb,
+                 const void* bias, void* out, int32_t* acc_dbg, int64_t M, int64_t N,
+                 int64_t K, int epilogue, void* stream);
+
+/* The convrot W8A8 linear: rotate + quantise the bf16/f16/f32 activation x [M,K] per
+ * token (BUTTERFLY order) into the caller's workspaces xq_ws (int8 [M,K]) and sx_ws
+ * (fp32 [M]), then slim_gemm_i8 against the pre-rotated weight codes qw [N,K] with row
+ * scales sw [N]. Drop-in for comfy_kitchen.int8_linear(x, qweight, wscales, convrot=True,
+ * convrot_groupsize=256, out_dtype=bf16) (tools/bench_int8.py:65-68). */
+int slim_int8_linear(const void* x, int x_dtype, const int8_t* qw, const float* sw,
+                     const void* bias, void* out, int8_t* xq_ws, float* sx_ws, int64_t M,
+                     int64_t N, int64_t K, int group, int epilogue, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SLIMDIT_B200_H_ */

@@ -1,0 +1,166 @@
+"""GPU parity of the tcgen05 INT8 GEMM and the convrot linear.
+
+* INT32 accumulators: bit-exact against exact integer math (oracle.int8_gemm_i32).
+* bf16 output: |y - ref| <= 1 bf16 ulp of ref, ref = fp64 dequant (acc * sa * sb + bias).
+* GELU epilogue: within 2 bf16 ulp of GELU(bf16(linear)) evaluated in fp32 on the CPU.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import synthetic
+
+pytestmark = pytest.mark.gpu
+
+
+def rand_i8(rng, shape):
+    return rng.integers(-127, 128, size=shape, dtype=np.int8)
+
+
+def check_bf16_within_one_ulp(y_bf16: torch.Tensor, ref: np.ndarray, what: str = "", term: np.ndarray | None = None):
+    """|y - ref| <= 1 bf16 ulp(ref) + 2^-21 |term|; term = the acc*sa*sb product whose fp32
+    rounding (int->float, scale product, fused multiply-add) matters only where the bias
+    cancels it to near zero."""
+    y = y_bf16.float().cpu().numpy().astype(np.float64)
+    err = np.abs(y - ref)
+    ulp = oracle.bf16_ulp(ref)
+    if term is not None:
+        ulp = ulp + np.abs(term) * 2.0**-21
+    bad = err > ulp
+    assert not bad.any(), f"{what}: {int(bad.sum())} outputs beyond 1 bf16 ulp; worst {float((err / ulp).max()):.3f} ulp"
+
+
+@pytest.mark.parametrize("m,n,k", [
+    (128, 256, 128),      # one tile, one k-block
+    (256, 512, 5120),     # several tiles, config K
+    (300, 264, 384),      # ragged M and N tails (N % 256 != 0), 3 k-blocks
+    (1, 8, 16),           # minimal: K and N below one tile, TMA zero fill
+    (129, 520, 1040),     # K not a multiple of 128
+    (1024, 1024, 13824),  # FFN down-proj K
+])
+def test_gemm_int32_accumulators_bit_exact_and_bf16_epilogue(cuda, m, n, k):
+    from slimdit import ops
+    rng = np.random.default_rng(m * 7 + n * 3 + k)
+    a, b = rand_i8(rng, (m, k)), rand_i8(rng, (n, k))
+    sa = (rng.random(m, dtype=np.float32) * 0.02 + 1e-3).astype(np.float32)
+    sb = (rng.random(n, dtype=np.float32) * 0.002 + 1e-4).astype(np.float32)
+    bias = synthetic.bf16_round_f32(rng.standard_normal(n).astype(np.float32) * 0.02)
+    at, bt = torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda)
+    y, acc = ops.gemm_i8(at, bt, torch.from_numpy(sa), torch.from_numpy(sb),
+                         torch.from_numpy(bias).to(torch.bfloat16), return_acc=True)
+    acc_ref = oracle.int8_gemm_i32(a, b)
+    assert np.array_equal(acc.cpu().numpy(), acc_ref)
+    check_bf16_within_one_ulp(y, oracle.linear_reference_f64(acc_ref, sa, sb, bias), "scale+bias",
+                              term=oracle.linear_reference_f64(acc_ref, sa, sb, None))
+    y2 = ops.gemm_i8(at, bt, torch.from_numpy(sa), torch.from_numpy(sb))
+    check_bf16_within_one_ulp(y2, oracle.linear_reference_f64(acc_ref, sa, sb, None), "scale only")
+
+
+def test_gemm_extreme_codes_saturate_nothing(cuda):
+    """All -128 / 127 codes at K=13824: |acc| up to 2.26e8 < 2^31 is exact."""
+    from slimdit import ops
+    m, n, k = 128, 256, 13824
+    a = np.full((m, k), -128, np.int8)
+    b = np.full((n, k), -128, np.int8)
+    b[1::2] = 127
+    _, acc = ops.gemm_i8(torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda),
+                         torch.ones(m), torch.ones(n), return_acc=True)
+    assert np.array_equal(acc.cpu().numpy(), oracle.int8_gemm_i32(a, b))
+
+
+def test_gemm_gelu_epilogue(cuda):
+    from slimdit import ops
+    rng = np.random.default_rng(5)
+    m, n, k = 256, 512, 1024
+    a, b = rand_i8(rng, (m, k)), rand_i8(rng, (n, k))
+    sa = np.full(m, 0.01, np.float32)
+    sb = (rng.random(n, dtype=np.float32) * 1e-3).astype(np.float32)
+    y, acc = ops.gemm_i8(torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda), torch.from_numpy(sa),
+                         torch.from_numpy(sb), epilogue="gelu_tanh", return_acc=True)
+    acc = acc.cpu().numpy()
+    lin = oracle.bf16_round((acc.astype(np.float32) * (sa[:, None] * sb[None, :])).astype(np.float32))
+    ref = oracle.gelu_tanh_f32(lin).astype(np.float64)
+    yv = y.float().cpu().numpy().astype(np.float64)
+    err = np.abs(yv - ref)
+    # 2 ulp: CUDA tanhf and numpy's float32 tanh may differ in the last fp32 bit, which can
+    # move the bf16 rounding of the GELU output by one step.
+    assert np.all(err <= 2 * oracle.bf16_ulp(ref) + 1e-30)
+
+
+def test_gemm_shape_errors(cuda):
+    from slimdit import ops
+    a = torch.zeros((4, 64), dtype=torch.int8, device=cuda)
+    with pytest.raises(ValueError):
+        ops.gemm_i8(a, torch.zeros((12, 64), dtype=torch.int8, device=cuda), torch.ones(4), torch.ones(12))
+    with pytest.raises(ValueError):
+        ops.gemm_i8(a, torch.zeros((16, 32), dtype=torch.int8, device=cuda), torch.ones(4), torch.ones(16))
+    y = ops.gemm_i8(a[:0], torch.zeros((16, 64), dtype=torch.int8, device=cuda), torch.ones(0), torch.ones(16))
+    assert y.shape == (0, 16)
+    from slimdit import _native
+    assert _native.device_error() == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 768, 5120), (77, 512, 1024), (4096, 1536, 5120)])
+def test_int8_linear_end_to_end_vs_oracle(cuda, m, n, k):
+    """x bf16 -> butterfly rotate + per-token INT8 -> GEMM -> bf16; weights from the reference
+    converter path. Codes bit-exact with the oracle's; output within 1 bf16 ulp of the fp64
+    dequant of those codes."""
+    from slimdit import ops
+    from slimdit.int8 import quantize_convrot_weight
+    x = synthetic.activations(m, k, seed=m + n)
+    w = synthetic.weight(n, k, seed=n + k)
+    bias = synthetic.bf16_round_f32(np.random.default_rng(1).standard_normal(n).astype(np.float32) * 0.02)
+    qw, sw = quantize_convrot_weight(w)
+    xt = torch.from_numpy(x).to(cuda).to(torch.bfloat16)
+    y = ops.int8_linear(xt, torch.from_numpy(qw).to(cuda), torch.from_numpy(sw).to(cuda),
+                        bias=torch.from_numpy(bias).to(cuda).to(torch.bfloat16))
+    assert y.dtype == torch.bfloat16 and y.shape == (m, n)
+    qx, sx = oracle.quantize_activations(x)
+    acc = oracle.int8_gemm_i32(qx, qw)
+    check_bf16_within_one_ulp(y, oracle.linear_reference_f64(acc, sx.reshape(-1), sw.reshape(-1), bias), "linear",
+                              term=oracle.linear_reference_f64(acc, sx.reshape(-1), sw.reshape(-1), None))
+    # accuracy of the whole convrot linear against the unquantised bf16 product
+    exact = x.astype(np.float64) @ w.astype(np.float64).T + bias
+    rel = np.linalg.norm(y.float().cpu().numpy() - exact) / np.linalg.norm(exact)
+    assert rel < 0.05
+
+
+def test_int8_linear_3d_input_and_out_dtype(cuda):
+    from slimdit import ops
+    from slimdit.int8 import quantize_convrot_weight
+    x = synthetic.activations(2 * 33, 512, seed=3).reshape(2, 33, 512)
+    w = synthetic.weight(256, 512, seed=4)
+    qw, sw = quantize_convrot_weight(w)
+    xt = torch.from_numpy(x).to(cuda).to(torch.bfloat16)
+    y = ops.int8_linear(xt, torch.from_numpy(qw).to(cuda), torch.from_numpy(sw).to(cuda), out_dtype=torch.float32)
+    assert y.shape == (2, 33, 256) and y.dtype == torch.float32
+    y2 = ops.int8_linear(xt.reshape(66, 512), torch.from_numpy(qw).to(cuda), torch.from_numpy(sw).to(cuda))
+    assert torch.equal(y.reshape(66, 256).to(torch.bfloat16), y2)
+
+
+def test_ffn_pair_vs_oracle(cuda):
+    """up-proj -> GELU-tanh -> rotate + requant -> down-proj, against the same pipeline on the
+    CPU (oracle codes, exact int32 GEMMs, fp32 GELU): outputs within 2 bf16 ulp + the effect
+    of hidden codes that differ by GELU rounding (checked via relative error)."""
+    from slimdit import ops
+    from slimdit.int8 import quantize_convrot_weight
+    m, hdim, f = 256, 512, 1024
+    x = synthetic.activations(m, hdim, seed=11)
+    wu, wd = synthetic.weight(f, hdim, seed=12), synthetic.weight(hdim, f, seed=13)
+    qu, su = quantize_convrot_weight(wu)
+    qd, sd = quantize_convrot_weight(wd)
+    dev = cuda
+    y = ops.ffn_int8(torch.from_numpy(x).to(dev).to(torch.bfloat16), torch.from_numpy(qu).to(dev),
+                     torch.from_numpy(su).to(dev), torch.from_numpy(qd).to(dev), torch.from_numpy(sd).to(dev))
+    qx, sx = oracle.quantize_activations(x)
+    acc1 = oracle.int8_gemm_i32(qx, qu)
+    h = oracle.bf16_round(oracle.gelu_tanh_f32(oracle.bf16_round(
+        (acc1.astype(np.float32) * (sx.reshape(-1, 1) * su.reshape(1, -1))).astype(np.float32))))
+    qh, sh = oracle.quantize_activations(h)
+    acc2 = oracle.int8_gemm_i32(qh, qd)
+    ref = oracle.linear_reference_f64(acc2, sh.reshape(-1), sd.reshape(-1), None)
+    yv = y.float().cpu().numpy()
+    rel = np.linalg.norm(yv - ref) / np.linalg.norm(ref)
+    assert rel < 1e-2, rel

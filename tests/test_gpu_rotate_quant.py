@@ -1,0 +1,157 @@
+"""GPU parity of the rotation / quantisation kernels against the reference's golden
+outputs and the oracle, through the C ABI (ops.* call libslimdit_b200.so directly)."""
+
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import synthetic
+
+pytestmark = pytest.mark.gpu
+
+WEIGHT_CASES = ["w_k256", "w_k512", "w_k768", "w_k1024", "w_k1280", "w_k5120", "w_k13824"]
+
+
+def bits(a):
+    return np.ascontiguousarray(a).view(np.uint32)
+
+
+def bf16_tensor(bits16: np.ndarray, device) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(bits16).view(np.int16)).to(device).view(torch.bfloat16)
+
+
+@pytest.mark.parametrize("name", WEIGHT_CASES)
+def test_weight_codes_scales_rotation_bit_exact_vs_reference(cuda, golden, name):
+    from slimdit import ops
+    x = bf16_tensor(golden[f"{name}_in_bf16"], cuda)
+    q, s, rot = ops.rotate_quant(x, order="reference", return_rotated=True)
+    assert np.array_equal(q.cpu().numpy(), golden[f"{name}_q"])
+    assert np.array_equal(bits(s.cpu().numpy()), bits(golden[f"{name}_scale"]))
+    assert np.array_equal(bits(rot.cpu().numpy()), bits(golden[f"{name}_rot"]))
+    # fused path (no rotated copy) gives the same codes
+    q2, s2 = ops.rotate_quant(x, order="reference")
+    assert torch.equal(q2, q) and torch.equal(s2, s)
+
+
+@pytest.mark.parametrize("name", WEIGHT_CASES)
+def test_numpy_api_drop_in_matches_reference(cuda, golden, name):
+    from slimdit.hadamard import build_hadamard, rotate
+    from slimdit.int8 import quantize_convrot_weight
+    w = synthetic.bf16_bits_to_f32(golden[f"{name}_in_bf16"])
+    q, s = quantize_convrot_weight(w)
+    assert q.dtype == np.int8 and s.dtype == np.float32 and s.shape == (w.shape[0], 1)
+    assert np.array_equal(q, golden[f"{name}_q"])
+    assert np.array_equal(bits(s), bits(golden[f"{name}_scale"]))
+    r = rotate(w, build_hadamard(256), 256)
+    assert np.array_equal(bits(r), bits(golden[f"{name}_rot"]))
+
+
+@pytest.mark.parametrize("name", ["w_k512", "w_k5120"])
+def test_dequantize_bit_exact_vs_reference(cuda, golden, name):
+    from slimdit.int8 import dequantize_convrot_weight
+    d = dequantize_convrot_weight(golden[f"{name}_q"], golden[f"{name}_scale"])
+    assert np.array_equal(bits(d), bits(golden[f"{name}_deq"]))
+
+
+def test_config0_full_weight_bit_exact(cuda, golden_meta):
+    """Config 0: W bf16 [5120, 5120] ~ N(0, 0.02), 5 outlier channels x50 -> codes and scales
+    identical to the reference's quantize_convrot_weight (SHA-256)."""
+    from slimdit import ops
+    meta = golden_meta["config0"]
+    w0 = synthetic.weight(5120, 5120, seed=0)
+    b16 = synthetic.f32_to_bf16_bits(w0)
+    assert hashlib.sha256(b16.tobytes()).hexdigest() == meta["sha256_input_bf16"]
+    q, s = ops.rotate_quant(bf16_tensor(b16, cuda), order="reference")
+    assert hashlib.sha256(q.cpu().numpy().tobytes()).hexdigest() == meta["sha256_q"]
+    assert hashlib.sha256(s.cpu().numpy().tobytes()).hexdigest() == meta["sha256_scale"]
+
+
+@pytest.mark.parametrize("rows,k", [(1, 256), (3, 512), (5, 1024), (7, 1280), (33, 5120), (4, 13824), (2, 16384),
+                                    (2, 20480)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_reference_order_vs_oracle_shapes_and_dtypes(cuda, rows, k, dtype):
+    from slimdit import ops
+    x = synthetic.activations(rows, k, seed=rows * 31 + k)
+    xt = torch.from_numpy(x).to(cuda).to(dtype)
+    xin = xt.float().cpu().numpy()
+    q, s, rot = ops.rotate_quant(xt, order="reference", return_rotated=True)
+    ref_rot = oracle.rotate_reference(xin)
+    qo, so = oracle.quantize_rows(ref_rot)
+    assert np.array_equal(bits(rot.cpu().numpy()), bits(ref_rot))
+    assert np.array_equal(q.cpu().numpy(), qo)
+    assert np.array_equal(bits(s.cpu().numpy()), bits(so))
+    q2, s2 = ops.rotate_quant(xt, order="reference")
+    assert torch.equal(q2, q) and torch.equal(s2, s)
+
+
+@pytest.mark.parametrize("rows,k", [(1, 256), (3, 512), (9, 768), (64, 5120), (17, 13824), (5, 16384)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+def test_butterfly_bit_exact_vs_oracle(cuda, rows, k, dtype):
+    from slimdit import ops
+    x = synthetic.activations(rows, k, seed=rows + k)
+    xt = torch.from_numpy(x).to(cuda).to(dtype)
+    xin = xt.float().cpu().numpy()
+    q, s, rot = ops.rotate_quant(xt, order="butterfly", return_rotated=True)
+    ref_rot = oracle.rotate_butterfly(xin)
+    qo, so = oracle.quantize_rows(ref_rot)
+    assert np.array_equal(bits(rot.cpu().numpy()), bits(ref_rot))
+    assert np.array_equal(q.cpu().numpy(), qo)
+    assert np.array_equal(bits(s.cpu().numpy()), bits(so))
+
+
+@pytest.mark.parametrize("name", ["x_k5120", "x_k13824"])
+def test_butterfly_within_tolerance_of_reference_rotation(cuda, golden, name):
+    """Activation order vs the reference's own rotation: |diff| <= 2^-20 * row absmax, codes +-1."""
+    from slimdit import ops
+    x = bf16_tensor(golden[f"{name}_in_bf16"], cuda)
+    q, s, rot = ops.rotate_quant(x, order="butterfly", return_rotated=True)
+    ref = golden[f"{name}_rot"]
+    tol = np.abs(ref).max(axis=1, keepdims=True) * 2.0**-20
+    assert np.all(np.abs(rot.cpu().numpy() - ref) <= tol)
+    assert np.abs(q.cpu().numpy().astype(np.int32) - golden[f"{name}_q"]).max() <= 1
+
+
+def test_quantize_stage_bit_exact_given_reference_rotation(cuda, golden):
+    """Quantisation alone, fed the reference's own rotated fp32 rows."""
+    from slimdit import ops
+    for name in ["w_k5120", "x_k5120", "x_k13824", "w_k256"]:
+        rot = torch.from_numpy(golden[f"{name}_rot"]).to(cuda)
+        q, s = ops.quantize_rows(rot)
+        assert np.array_equal(q.cpu().numpy(), golden[f"{name}_q"]), name
+        assert np.array_equal(bits(s.cpu().numpy()), bits(golden[f"{name}_scale"])), name
+
+
+def test_edge_rows_zero_constant_and_huge(cuda):
+    from slimdit import ops
+    k = 1280
+    x = np.zeros((6, k), np.float32)
+    x[1] = 1.0                      # constant row
+    x[2, 7] = -3.0                  # single spike
+    x[3] = np.float32(1e35)         # large but finite through the whole chain
+    x[4, ::2] = 1e-30               # tiny
+    x[5] = synthetic.activations(1, k, seed=9)[0]
+    for order, rot_fn in (("reference", oracle.rotate_reference), ("butterfly", oracle.rotate_butterfly)):
+        q, s, rot = ops.rotate_quant(torch.from_numpy(x).to(cuda), order=order, return_rotated=True)
+        ro = rot_fn(x)
+        qo, so = oracle.quantize_rows(ro)
+        assert np.array_equal(bits(rot.cpu().numpy()), bits(ro)), order
+        assert np.array_equal(q.cpu().numpy(), qo), order
+        assert np.array_equal(bits(s.cpu().numpy()), bits(so)), order
+    assert s.cpu().numpy()[0, 0] == np.float32(1e-30)
+
+
+def test_empty_and_error_cases(cuda):
+    from slimdit import ops
+    q, s = ops.rotate_quant(torch.empty((0, 512), device=cuda, dtype=torch.bfloat16))
+    assert q.shape == (0, 512) and s.shape == (0, 1)
+    with pytest.raises(ValueError):
+        ops.rotate_quant(torch.zeros((2, 300), device=cuda))
+    with pytest.raises(ValueError):
+        ops.rotate_quant(torch.zeros((2, 512), device=cuda), group_size=128)
+    with pytest.raises(ValueError):
+        ops.rotate_quant(torch.zeros((2, 32768), device=cuda, dtype=torch.bfloat16), order="butterfly")
+    from slimdit import _native
+    assert _native.device_error() == 0

@@ -1,0 +1,342 @@
+// INT8 x INT8 -> INT32 GEMM on the sm_100a 5th-generation tensor cores (tcgen05 kind::i8)
+// with a dequantising epilogue:
+//
+//   out[m, n] = bf16( float(sum_k A[m,k] * B[n,k]) * (sa[m] * sb[n]) + bias[n] )
+//
+// which is the runtime side of the convrot linear: `x_rot @ (q * scale)^T` with the
+// activation quantised per token (slimdit/int8.py:9-11; the runtime op that the reference
+// calls is comfy_kitchen.int8_linear, tools/bench_int8.py:65-68). A is the token matrix, B
+// the weight codes; both are K-major (row-major with K contiguous), i.e. a "TN" GEMM.
+//
+// Structure (one CTA per SM, persistent over output tiles of 128 x 256):
+//   warp 0      TMA producer: 128x128-byte A and 256x128-byte B tiles, 128-byte swizzle,
+//               4-stage shared-memory ring guarded by full/empty mbarriers.
+//   warp 1      allocates 512 TMEM columns (two 256-column int32 accumulators) and one
+//               lane issues tcgen05.mma (M=128, N=256, K=32 per instruction, 4 per stage),
+//               committing to the ring's empty barriers and to the accumulator barriers.
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator rows (warp w owns TMEM lanes
+//               32*(w%4)..+31), scale/bias/GELU in fp32, bf16 stores; double-buffered
+//               accumulators let the next tile's MMAs run under this epilogue.
+// Every mbarrier wait is bounded (slim_ptx.cuh); on a timeout the kernel records an error,
+// drains its own TMA loads and MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "slim_kernels.h"
+#include "slim_ptx.cuh"
+
+namespace slim {
+namespace gi8 {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // bytes == int8 elements: one 128-byte swizzle row
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK;
+constexpr int B_BYTES = BN * BK;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int GROUP_M = 16;
+constexpr int MMA_K = 32;
+constexpr uint32_t IDESC = idesc_i8(BM, BN);
+
+struct Shared {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  volatile int abort;
+};
+
+constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + sizeof(Shared) + 64;
+
+__device__ __forceinline__ void tile_coords(int64_t t, int tiles_m, int tiles_n, int& tm, int& tn) {
+  const int64_t per_group = static_cast<int64_t>(GROUP_M) * tiles_n;
+  const int64_t g = t / per_group;
+  const int first_m = static_cast<int>(g * GROUP_M);
+  const int gm = min(tiles_m - first_m, GROUP_M);
+  const int local = static_cast<int>(t - g * per_group);
+  tm = first_m + local % gm;
+  tn = local / gm;
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float kBeta = 0.7978845608028654f;  // sqrt(2/pi)
+  const float kKappa = 0.044715f;
+  const float inner = kBeta * (x + kKappa * x * x * x);
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float bf16_round(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_i8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+               const GemmI8Params p, int tiles_m, int tiles_n) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  Shared& sh = *reinterpret_cast<Shared*>(smem + STAGES * STAGE_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t total_tiles = static_cast<int64_t>(tiles_m) * tiles_n;
+  const int num_kb = static_cast<int>((p.K + BK - 1) / BK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sh.tfull[a], 1);
+      mbar_init(&sh.tempty[a], 128);
+    }
+    mbar_init(&sh.drain, 1);
+    sh.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sh.tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = sh.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tma_a);
+      tma_prefetch_desc(&tma_b);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, last_parity = 0;
+      for (int64_t t = blockIdx.x; t < total_tiles && !sh.abort; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, tiles_m, tiles_n, tm, tn);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&sh.empty[stage], phase ^ 1, kErrWaitTimeoutProducer)) {
+            sh.abort = 1;
+            break;
+          }
+          if (sh.abort) break;
+          mbar_arrive_expect_tx(&sh.full[stage], STAGE_BYTES);
+          tma_load_2d(sA + stage * A_BYTES, &tma_a, &sh.full[stage], kb * BK, tm * BM);
+          tma_load_2d(sB + stage * B_BYTES, &tma_b, &sh.full[stage], kb * BK, tn * BN);
+          issued |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Every load this thread issued must land before the CTA may exit.
+      for (int s = 0; s < STAGES; ++s)
+        if (issued & (1u << s)) mbar_wait(&sh.full[s], (last_parity >> s) & 1, kErrWaitTimeoutDrain);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int as = 0;
+      uint32_t aphase = 0;
+      bool issued_any = false;
+      for (int64_t t = blockIdx.x; t < total_tiles && !sh.abort; t += gridDim.x) {
+        if (!mbar_wait(&sh.tempty[as], aphase ^ 1, kErrWaitTimeoutMma)) {
+          sh.abort = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(as * BN);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&sh.full[stage], phase, kErrWaitTimeoutMma) || sh.abort) {
+            sh.abort = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / MMA_K; ++kk) {
+            mma_i8(d, smem_desc_sw128(a0 + kk * MMA_K), smem_desc_sw128(b0 + kk * MMA_K), IDESC,
+                   (kb | kk) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          mma_commit(&sh.empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&sh.tfull[as]);
+        as ^= 1;
+        if (as == 0) aphase ^= 1;
+      }
+      // All issued MMAs must complete before TMEM is released.
+      if (issued_any) {
+        mma_commit(&sh.drain);
+        mbar_wait(&sh.drain, 0, kErrWaitTimeoutDrain);
+      }
+    }
+    __syncwarp();
+  } else {
+    // epilogue warps 2..5
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    int as = 0;
+    uint32_t aphase = 0;
+    const __nv_bfloat16* bias = static_cast<const __nv_bfloat16*>(p.bias);
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+    for (int64_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      bool ok = mbar_wait(&sh.tfull[as], aphase, kErrWaitTimeoutEpilogue);
+      ok = __all_sync(0xffffffffu, ok) && !sh.abort;
+      if (!ok) {
+        sh.abort = 1;
+        break;
+      }
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, tm, tn);
+      const int64_t m = static_cast<int64_t>(tm) * BM + row;
+      const bool row_ok = m < p.M;
+      const float sam = row_ok ? __ldg(p.sa + m) : 0.0f;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(as * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + c * 32, r);
+        tmem_ld_wait();
+        const int64_t n0 = static_cast<int64_t>(tn) * BN + c * 32;
+        if (row_ok) {
+          if (p.acc_dbg != nullptr) {
+            int32_t* dst = p.acc_dbg + m * p.N + n0;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              if (n0 + j < p.N)
+                *reinterpret_cast<int4*>(dst + j) = make_int4(static_cast<int>(r[j]), static_cast<int>(r[j + 1]),
+                                                              static_cast<int>(r[j + 2]), static_cast<int>(r[j + 3]));
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            if (n0 + j >= p.N) break;
+            const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j));
+            const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j + 4));
+            const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+            float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (bias != nullptr) {
+              const uint4 bu = __ldg(reinterpret_cast<const uint4*>(bias + n0 + j));
+              const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                bv[2 * e] = __uint_as_float(bw[e] << 16);
+                bv[2 * e + 1] = __uint_as_float(bw[e] & 0xffff0000u);
+              }
+            }
+            float y[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float acc = static_cast<float>(static_cast<int>(r[j + e]));
+              y[e] = __fmaf_rn(acc, sam * sv[e], bv[e]);
+              if (p.epilogue == kEpiGeluTanh) y[e] = gelu_tanh(bf16_round(y[e]));
+            }
+            uint4 o;
+            o.x = pack_bf16x2(y[0], y[1]);
+            o.y = pack_bf16x2(y[2], y[3]);
+            o.z = pack_bf16x2(y[4], y[5]);
+            o.w = pack_bf16x2(y[6], y[7]);
+            *reinterpret_cast<uint4*>(out + m * p.ldo + n0 + j) = o;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sh.tempty[as]);
+      as ^= 1;
+      if (as == 0) aphase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace gi8
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  if (fn == nullptr) {
+    void* sym = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &sym, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(sym);
+  }
+  return fn;
+}
+
+// 2-D K-major int8 operand [rows, K], box = 128 bytes of K x box_rows rows, 128-byte swizzle.
+static bool make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t K, int box_rows) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(gi8::BK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+cudaError_t launch_gemm_i8(const GemmI8Params& p, cudaStream_t st) {
+  CUtensorMap ma, mb;
+  if (!make_kmajor_map(&ma, p.a, p.M, p.K, gi8::BM)) return cudaErrorInvalidValue;
+  if (!make_kmajor_map(&mb, p.b, p.N, p.K, gi8::BN)) return cudaErrorInvalidValue;
+  const int tiles_m = static_cast<int>((p.M + gi8::BM - 1) / gi8::BM);
+  const int tiles_n = static_cast<int>((p.N + gi8::BN - 1) / gi8::BN);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t total = static_cast<int64_t>(tiles_m) * tiles_n;
+  const int grid = static_cast<int>(total < sms ? total : sms);
+  static bool attr_set[64] = {false};
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gi8::gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(gi8::SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  gi8::gemm_i8_kernel<<<grid, gi8::THREADS, gi8::SMEM_BYTES, st>>>(ma, mb, p, tiles_m, tiles_n);
+  return cudaGetLastError();
+}
+
+}  // namespace slim

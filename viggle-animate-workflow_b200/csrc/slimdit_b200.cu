@@ -1,0 +1,5 @@
+// Single translation unit of libslimdit_b200.so: the kernel files share the device error
+// word (slim::g_device_error) without relocatable device code.
+#include "capi.cu"
+#include "gemm_i8.cu"
+#include "rotate_quant.cu"

@@ -1,0 +1,191 @@
+"""Device entry points on torch CUDA tensors (memory comes from torch's allocator; every
+computation runs in libslimdit_b200.so).
+
+* ``rotate_quant``  group-256 Hadamard rotation + per-row INT8 (slimdit/int8.py:39-52 for
+  weights in the reference order; the per-token activation side of the runtime linear in
+  the butterfly order)
+* ``rotate``        rotation alone, fp32 out (slimdit/hadamard.py:45-58)
+* ``quantize_rows`` quantisation alone (slimdit/int8.py:49-51)
+* ``dequantize``    (q * scale) @ H^T (slimdit/int8.py:55-61)
+* ``gemm_i8``       int8 GEMM + scale/bias(/GELU) epilogue
+* ``int8_linear``   the convrot W8A8 linear, same call shape as the runtime op the reference
+                    benchmarks (``comfy_kitchen.int8_linear``, tools/bench_int8.py:65-68)
+* ``ffn_int8``      up-proj -> GELU-tanh -> rotate + requant -> down-proj
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _native as nat
+
+_DT = {torch.float32: nat.F32, torch.bfloat16: nat.BF16, torch.float16: nat.F16}
+_ORDERS = {"reference": nat.ORDER_REFERENCE, "butterfly": nat.ORDER_BUTTERFLY}
+_EPI = {None: nat.EPI_SCALE_BIAS, "none": nat.EPI_SCALE_BIAS, "gelu_tanh": nat.EPI_GELU_TANH}
+
+
+def _cuda2d(t: torch.Tensor, name: str) -> torch.Tensor:
+    nat.require_cuda()
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+    if t.dim() != 2:
+        raise ValueError(f"expected a 2D {name}, got shape {tuple(t.shape)}")
+    return t.contiguous()
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def rotate_quant(x: torch.Tensor, group_size: int = 256, order: str = "reference",
+                 return_rotated: bool = False):
+    """Rotate [rows, K] (f32/bf16/f16) and quantise per row -> (int8 [rows, K], f32 [rows, 1][, f32 rotated])."""
+    x = _cuda2d(x, "input")
+    if x.dtype not in _DT:
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    if order not in _ORDERS:
+        raise ValueError(f"order must be one of {sorted(_ORDERS)}")
+    rows, k = x.shape
+    q = torch.empty((rows, k), dtype=torch.int8, device=x.device)
+    scale = torch.empty((rows, 1), dtype=torch.float32, device=x.device)
+    rot = torch.empty((rows, k), dtype=torch.float32, device=x.device) if return_rotated else None
+    with torch.cuda.device(x.device):
+        nat.check(nat.load().slim_rotate_quant_i8(x.data_ptr(), _DT[x.dtype], rows, k, group_size, _ORDERS[order],
+                                                  q.data_ptr(), scale.data_ptr(), _ptr(rot), _stream(x)))
+    return (q, scale, rot) if return_rotated else (q, scale)
+
+
+def rotate(x: torch.Tensor, group_size: int = 256) -> torch.Tensor:
+    """fp32 group-wise rotation W @ H^T in the reference order."""
+    x = _cuda2d(x, "weight")
+    if x.dtype not in _DT:
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    rows, k = x.shape
+    out = torch.empty((rows, k), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        nat.check(nat.load().slim_rotate_f32(x.data_ptr(), _DT[x.dtype], rows, k, group_size, nat.ORDER_REFERENCE,
+                                             out.data_ptr(), _stream(x)))
+    return out
+
+
+def quantize_rows(rotated: torch.Tensor):
+    """Per-row symmetric INT8 of fp32 rows -> (int8 [rows, K], f32 [rows, 1])."""
+    rotated = _cuda2d(rotated, "rotated")
+    if rotated.dtype != torch.float32:
+        raise TypeError("rotated rows must be float32")
+    rows, k = rotated.shape
+    q = torch.empty((rows, k), dtype=torch.int8, device=rotated.device)
+    scale = torch.empty((rows, 1), dtype=torch.float32, device=rotated.device)
+    with torch.cuda.device(rotated.device):
+        nat.check(nat.load().slim_quantize_rows_i8(rotated.data_ptr(), rows, k, q.data_ptr(), scale.data_ptr(),
+                                                   _stream(rotated)))
+    return q, scale
+
+
+def dequantize(q: torch.Tensor, scale: torch.Tensor, group_size: int = 256) -> torch.Tensor:
+    """(q * scale) @ H^T in the reference order -> fp32 [rows, K]."""
+    q = _cuda2d(q, "q")
+    if q.dtype != torch.int8:
+        raise TypeError("q must be int8")
+    rows, k = q.shape
+    scale = scale.to(device=q.device, dtype=torch.float32).contiguous().reshape(-1)
+    if scale.numel() != rows:
+        raise ValueError(f"scale has {scale.numel()} entries for {rows} rows")
+    out = torch.empty((rows, k), dtype=torch.float32, device=q.device)
+    with torch.cuda.device(q.device):
+        nat.check(nat.load().slim_dequant_i8(q.data_ptr(), scale.data_ptr(), rows, k, group_size, out.data_ptr(),
+                                             _stream(q)))
+    return out
+
+
+def _vec(t: torch.Tensor | None, n: int, dtype, device, name: str) -> torch.Tensor | None:
+    if t is None:
+        return None
+    t = t.to(device=device, dtype=dtype).contiguous().reshape(-1)
+    if t.numel() != n:
+        raise ValueError(f"{name} has {t.numel()} entries, expected {n}")
+    return t
+
+
+def gemm_i8(a: torch.Tensor, b: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: torch.Tensor | None = None,
+            epilogue: str | None = None, return_acc: bool = False, out: torch.Tensor | None = None):
+    """bf16(acc * sa[m] * sb[n] + bias[n]) (optionally GELU-tanh) for int8 a [M,K], b [N,K]."""
+    a = _cuda2d(a, "a")
+    b = _cuda2d(b, "b")
+    if a.dtype != torch.int8 or b.dtype != torch.int8:
+        raise TypeError("a and b must be int8")
+    m, k = a.shape
+    n, kb = b.shape
+    if k != kb:
+        raise ValueError(f"K mismatch: a {tuple(a.shape)} vs b {tuple(b.shape)}")
+    if epilogue not in _EPI:
+        raise ValueError(f"epilogue must be one of {sorted(str(e) for e in _EPI)}")
+    dev = a.device
+    sa = _vec(sa, m, torch.float32, dev, "sa")
+    sb = _vec(sb, n, torch.float32, dev, "sb")
+    bias = _vec(bias, n, torch.bfloat16, dev, "bias")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    elif out.shape != (m, n) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 [M, N] tensor")
+    acc = torch.empty((m, n), dtype=torch.int32, device=dev) if return_acc else None
+    with torch.cuda.device(dev):
+        nat.check(nat.load().slim_gemm_i8(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(), _ptr(bias),
+                                          out.data_ptr(), _ptr(acc), m, n, k, _EPI[epilogue], _stream(a)))
+    return (out, acc) if return_acc else out
+
+
+def int8_linear(x: torch.Tensor, qweight: torch.Tensor, wscales: torch.Tensor, convrot: bool = True,
+                convrot_groupsize: int = 256, out_dtype: torch.dtype = torch.bfloat16,
+                bias: torch.Tensor | None = None, epilogue: str | None = None) -> torch.Tensor:
+    """Convrot W8A8 linear: y = rot(x) quantised per token @ (qweight * wscales)^T + bias.
+
+    x: [..., K] bf16/f16/f32 CUDA; qweight: int8 [N, K] (pre-rotated, slimdit/int8.py:3-11);
+    wscales: f32 [N, 1] or [N]. Same call shape as the runtime op the reference uses
+    (tools/bench_int8.py:65-68). The output is computed in bf16 and cast if out_dtype differs.
+    """
+    nat.require_cuda()
+    if not x.is_cuda:
+        raise TypeError("x must be a CUDA tensor")
+    if x.dtype not in _DT:
+        raise TypeError(f"unsupported activation dtype {x.dtype}")
+    qweight = _cuda2d(qweight, "qweight")
+    k = x.shape[-1]
+    n = qweight.shape[0]
+    if qweight.shape[1] != k:
+        raise ValueError(f"in_features mismatch: x [..., {k}] vs qweight {tuple(qweight.shape)}")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, k).contiguous()
+    m = x2.shape[0]
+    dev = x2.device
+    sw = _vec(wscales, n, torch.float32, dev, "wscales")
+    b = _vec(bias, n, torch.bfloat16, dev, "bias")
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    if convrot:
+        xq = torch.empty((m, k), dtype=torch.int8, device=dev)
+        sx = torch.empty((m,), dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            nat.check(nat.load().slim_int8_linear(x2.data_ptr(), _DT[x2.dtype], qweight.data_ptr(), sw.data_ptr(),
+                                                  _ptr(b), out.data_ptr(), xq.data_ptr(), sx.data_ptr(), m, n, k,
+                                                  convrot_groupsize, _EPI[epilogue], _stream(x2)))
+    else:
+        xq, sx = quantize_rows(x2.float())
+        gemm_i8(xq, qweight, sx, sw, b, epilogue=epilogue, out=out)
+    out = out.reshape(*lead, n)
+    return out if out_dtype == torch.bfloat16 else out.to(out_dtype)
+
+
+def ffn_int8(x: torch.Tensor, w_up: torch.Tensor, s_up: torch.Tensor, w_down: torch.Tensor, s_down: torch.Tensor,
+             b_up: torch.Tensor | None = None, b_down: torch.Tensor | None = None) -> torch.Tensor:
+    """DiT FFN pair on the convrot linear: down(rotquant(gelu_tanh(up(x)))).
+
+    The up-projection's epilogue applies GELU-tanh to its bf16 output (the same rounding as
+    running the linear and then the activation on its bf16 result); the hidden activation
+    is rotated and requantised per token before the down-projection.
+    """
+    h = int8_linear(x, w_up, s_up, bias=b_up, epilogue="gelu_tanh")
+    return int8_linear(h, w_down, s_down, bias=b_down)
