@@ -47,8 +47,8 @@ NOMINAL_I8_TOPS = 4500.0
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -85,7 +85,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+                 "-lms", "100"], stdout=self.tmp, stderr=subprocess.DEVNULL)
         except (FileNotFoundError, OSError):
             self.proc = None
         time.sleep(0.3)
@@ -180,8 +180,8 @@ def cpu_baseline(target_seconds: float) -> dict:
         total_rows += rows
     value = 2.0 * total_rows * N * K / total_t / 1e12
     return {"value": round(value, 4), "unit": "TOPS", "cores": threads, "kind": "port",
-            "sample": f"{total_rows} of {M} tokens of the 32768x15360x5120 linear "
-                      f"(oracle rotation+quant, torch CPU int8 GEMM), {total_t:.1f} s"}
+            "sample": f"{total_rows} tokens in chunks of {rows} through the 15360x5120 linear "
+                      f"(oracle rotation+quant, torch CPU int8 GEMM), {total_t:.1f} s of CPU time"}
 
 
 def run_reference(args) -> int:
@@ -326,12 +326,11 @@ def run_ours(args) -> int:
             peak_src = "2 x fallback bf16 1.59 PFLOP/s"
         gemm_tops = OPS_PER_STEP / (gemm_ms * 1e-3) / 1e12
         traffic = None
-        prof = ROOT / "profiles" / "gemm_i8_traffic.json"
+        prof = ROOT / "profiles" / "gemm_i8_qkv_32768x15360x5120.md"
         if prof.exists():
-            try:
-                traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
-            except Exception:  # noqa: BLE001
-                traffic = None
+            for ln in prof.read_text().splitlines():
+                if ln.startswith("dram_bytes_per_launch:"):
+                    traffic = int(ln.split(":", 1)[1])
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": steps,
             "warmup": max(3, args.warmup), "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,

@@ -2,7 +2,8 @@
 
 * INT32 accumulators: bit-exact against exact integer math (oracle.int8_gemm_i32).
 * bf16 output: |y - ref| <= 1 bf16 ulp of ref, ref = fp64 dequant (acc * sa * sb + bias).
-* GELU epilogue: within 2 bf16 ulp of GELU(bf16(linear)) evaluated in fp32 on the CPU.
+* GELU epilogue: within 2 bf16 ulp (+ the tanh cancellation term) of GELU(bf16(linear))
+  evaluated in fp32 on the CPU.
 """
 
 import numpy as np
@@ -84,9 +85,12 @@ def test_gemm_gelu_epilogue(cuda):
     ref = oracle.gelu_tanh_f32(lin).astype(np.float64)
     yv = y.float().cpu().numpy().astype(np.float64)
     err = np.abs(yv - ref)
-    # 2 ulp: CUDA tanhf and numpy's float32 tanh may differ in the last fp32 bit, which can
-    # move the bf16 rounding of the GELU output by one step.
-    assert np.all(err <= 2 * oracle.bf16_ulp(ref) + 1e-30)
+    # CUDA tanhf and numpy's float32 tanh may differ by a few fp32 ulp. Near tanh = -1
+    # (x below about -3) 0.5*x*(1 + tanh) cancels, so such a difference is an absolute error
+    # of ~0.5*|x|*2^-24 per ulp, large relative to the tiny output; elsewhere it can move the
+    # bf16 rounding by one step. Tolerance: 2 bf16 ulp + 4 fp32 tanh ulp scaled by |x|.
+    tol = 2 * oracle.bf16_ulp(ref) + 4 * 2.0**-24 * np.abs(lin.astype(np.float64))
+    assert np.all(err <= tol), float((err / tol).max())
 
 
 def test_gemm_shape_errors(cuda):

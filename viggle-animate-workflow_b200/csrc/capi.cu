@@ -191,6 +191,7 @@ static int gemm_checks(const int8_t* a, const int8_t* b, const float* sa, const 
   if (N % 8 != 0) return fail(SLIM_ERR_SHAPE, "N=%lld must be a multiple of 8", static_cast<long long>(N));
   if (M > (int64_t{1} << 31) || N > (int64_t{1} << 31)) return fail(SLIM_ERR_SHAPE, "GEMM dimension too large");
   if (epilogue != kEpiScaleBias && epilogue != kEpiGeluTanh) return fail(SLIM_ERR_DTYPE, "unknown epilogue %d", epilogue);
+  if (M == 0) return SLIM_OK;  // empty problem: nothing is read or written
   if (a == nullptr || b == nullptr || sa == nullptr || sb == nullptr || out == nullptr) return fail(SLIM_ERR_NULL, "a/b/sa/sb/out is NULL");
   if (!aligned16(a) || !aligned16(b) || !aligned16(sb) || !aligned16(out) || (bias != nullptr && !aligned16(bias)) ||
       (acc_dbg != nullptr && !aligned16(acc_dbg)))
@@ -218,10 +219,10 @@ int slim_int8_linear(const void* x, int x_dtype, const int8_t* qw, const float* 
   if ((rc = check_group(K, group)) != SLIM_OK) return rc;
   if ((rc = check_dtype(x_dtype)) != SLIM_OK) return rc;
   if (K > 16384) return fail(SLIM_ERR_SHAPE, "in_features above 16384 not supported by the activation quantiser");
-  if (x == nullptr || xq_ws == nullptr || sx_ws == nullptr) return fail(SLIM_ERR_NULL, "x/xq_ws/sx_ws is NULL");
   if ((rc = gemm_checks(xq_ws, qw, sx_ws, sw, bias, out, nullptr, M, N, K, epilogue)) != SLIM_OK) return rc;
-  if (!aligned16(x)) return fail(SLIM_ERR_ALIGN, "x must be 16-byte aligned");
   if (M == 0) return SLIM_OK;
+  if (x == nullptr) return fail(SLIM_ERR_NULL, "x is NULL");
+  if (!aligned16(x)) return fail(SLIM_ERR_ALIGN, "x must be 16-byte aligned");
   if ((rc = check_arch()) != SLIM_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = launch_bfly_rotate_quant(x, x_dtype, M, static_cast<int>(K), xq_ws, sx_ws, nullptr, st);
