@@ -105,6 +105,22 @@ int slim_int8_linear(const void* x, int x_dtype, const int8_t* qw, const float* 
                      const void* bias, void* out, int8_t* xq_ws, float* sx_ws, int64_t M,
                      int64_t N, int64_t K, int group, int epilogue, void* stream);
 
+/* The convrot linear without caller workspaces, for callers that cannot allocate device
+ * memory: code running inside a host framework that owns the device memory pool (a plugin
+ * given only its inputs and outputs), or on a path where an allocation would synchronise
+ * or fail under a memory cap. No counterpart exists in the reference (its runtime op
+ * allocates through torch).
+ * Same arguments and result as slim_int8_linear, minus xq_ws/sx_ws: the activation codes
+ * and scales go to one 32 MiB array compiled into the library, which every GPU that loads
+ * the library holds until exit. Limit: round_up(M*K, 256) + 4*M <= 32 MiB (e.g. 6400
+ * tokens at K = 5120); larger calls return SLIM_ERR_SHAPE. The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress); make it before any stream
+ * capture. All calls share the array: calls that overlap on the GPU race. Allocates
+ * nothing (no cudaMalloc/cudaFree). */
+int slim_int8_linear_noalloc(const void* x, int x_dtype, const int8_t* qw, const float* sw,
+                             const void* bias, void* out, int64_t M, int64_t N, int64_t K,
+                             int group, int epilogue, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

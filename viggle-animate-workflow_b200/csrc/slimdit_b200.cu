@@ -3,3 +3,4 @@
 #include "capi.cu"
 #include "gemm_i8.cu"
 #include "rotate_quant.cu"
+#include "linear_noalloc.cu"
