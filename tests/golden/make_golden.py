@@ -11,8 +11,8 @@ inputs (tests/synthetic.py):
   * dequantize_convrot_weight outputs;
   * per-token activation quantisation with the reference's own math (rotate + int8.py:49-51);
   * SHA-256 of the full config-0 weight conversion (W [5120, 5120]);
-  * the descriptor blob, and the bytes (SHA-256 + header) of a reference convert() run on a
-    2-block synthetic official checkpoint.
+  * the descriptor blob, and the bytes (SHA-256 + header) of reference convert() runs on a
+    2-block synthetic official checkpoint (full, and with block_limit=0).
 The GPU box has no reference tree: tests read only these fixtures.
 """
 
@@ -110,6 +110,13 @@ def main(argv=None) -> int:
             "quant_errors": [float(e) for e in report.quant_errors],
             "src_sha256": {p.name: sha256(p.read_bytes()) for p in sorted(Path(src).glob("*.safetensors"))},
         }
+        # block_limit=0: every host-side tensor (copies, concat, curves, table, rope) and no
+        # quantised linear -- checkable without a GPU.
+        out0 = Path(tmp) / "out_block0.safetensors"
+        ref_convert.convert(src, out0, rank=8, grid=65, block_limit=0)
+        raw0 = out0.read_bytes()
+        meta["convert_block0"] = {"case": CONVERT_CASE, "rank": 8, "grid": 65, "block_limit": 0,
+                                  "sha256_file": sha256(raw0), "size": len(raw0)}
     (HERE / "golden.json").write_text(json.dumps(meta, indent=1, sort_keys=True))
     print("wrote", HERE / "rotation_quant.npz", HERE / "golden.json")
     return 0
