@@ -155,3 +155,29 @@ def test_empty_and_error_cases(cuda):
         ops.rotate_quant(torch.zeros((2, 32768), device=cuda, dtype=torch.bfloat16), order="butterfly")
     from slimdit import _native
     assert _native.device_error() == 0
+
+
+def test_butterfly_quantiser_near_rounding_boundaries(cuda):
+    """Rows whose rotated values sit on or next to half-integer multiples of the row scale:
+    the quantiser's reciprocal fast path must hand these to the exact division."""
+    from slimdit import ops
+    rng = np.random.default_rng(77)
+    k = 5120
+    rows = []
+    for r in range(48):
+        target = (rng.integers(-127, 127, size=k) + 0.5).astype(np.float64)
+        target[0] = 127.0
+        target *= 10.0 ** rng.uniform(-3, 2) / 127.0
+        # pre-image under the rotation (H is its own inverse); fp32 inputs keep the ties
+        rows.append(oracle.rotate_reference(target.astype(np.float32)[None])[0])
+    x = np.stack(rows)
+    xt = torch.from_numpy(x).to(cuda)
+    q, s, rot = ops.rotate_quant(xt, order="butterfly", return_rotated=True)
+    ro = oracle.rotate_butterfly(x)
+    qo, so = oracle.quantize_rows(ro)
+    assert np.array_equal(bits(rot.cpu().numpy()), bits(ro))
+    assert np.array_equal(bits(s.cpu().numpy()), bits(so))
+    assert np.array_equal(q.cpu().numpy(), qo)
+    # the construction really produced near-ties
+    frac = np.abs(ro / so - np.round(ro / so))
+    assert (np.abs(frac - 0.5) < 1e-3).mean() > 0.1

@@ -32,6 +32,7 @@
 #include <cstdint>
 
 #include "slim_kernels.h"
+#include "slim_ptx.cuh"
 
 namespace slim {
 
@@ -255,133 +256,258 @@ __global__ void __launch_bounds__(256) ref_rotate_kernel(const void* __restrict_
   }
 }
 
-// ------------------------------------------------------------------ butterfly order
-// radix-4 butterfly on (a0,a1,a2,a3) in place.
-__device__ __forceinline__ void bfly4(float& a0, float& a1, float& a2, float& a3) {
-  const float s = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
-  const float b0 = __fmaf_rn(-2.0f, a3, s);
-  const float b1 = __fmaf_rn(-2.0f, a2, s);
-  const float b2 = __fmaf_rn(-2.0f, a1, s);
-  const float b3 = __fmaf_rn(-2.0f, a0, s);
+// ------------------------------------------------------------------ butterfly, packed pairs
+// Packed fp32x2 arithmetic (sm_100): each lane is an independent IEEE-rounded fp32 op, so a
+// pair of values goes through exactly the rounding steps of the scalar code.
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// bfly4 on pairs: b_i = ((a0 + a1) + (a2 + a3)) - 2*a_{3-i} in each lane.
+__device__ __forceinline__ void bfly4x2(float2& a0, float2& a1, float2& a2, float2& a3) {
+  const float2 m2 = make_float2(-2.0f, -2.0f);
+  const float2 s = add2(add2(a0, a1), add2(a2, a3));
+  const float2 b0 = fma2(m2, a3, s), b1 = fma2(m2, a2, s), b2 = fma2(m2, a1, s), b3 = fma2(m2, a0, s);
   a0 = b0; a1 = b1; a2 = b2; a3 = b3;
 }
 
-// Digits 0 and 1 of a 16-element chunk held in registers (index i = 4*d1 + d0).
-__device__ __forceinline__ void bfly16(float (&v)[16]) {
+__device__ __forceinline__ void bfly16x2(float2 (&v)[16]) {
 #pragma unroll
-  for (int q = 0; q < 4; ++q) bfly4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  for (int q = 0; q < 4; ++q) bfly4x2(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
 #pragma unroll
-  for (int m = 0; m < 4; ++m) bfly4(v[m], v[4 + m], v[8 + m], v[12 + m]);
+  for (int m = 0; m < 4; ++m) bfly4x2(v[m], v[4 + m], v[8 + m], v[12 + m]);
 }
 
-constexpr int kGroupPad = 272;  // floats per group in the exchange buffer (256 + 16)
-
-// Swizzled position of element (r, i) of a group in the exchange buffer: row r holds the
-// 16 values of chunk r; float4 slots are XOR-permuted by (r>>1)&3 so both the row-wise
-// float4 writes and the column-wise reads are bank-conflict free.
-__device__ __forceinline__ int xpos(int r, int i) {
-  return 16 * r + 4 * (((i >> 2) ^ (r >> 1)) & 3) + (i & 3);
+// Exchange buffer of one group pair: 16 rows (chunks) x 16 float2; 16-byte slots of a row
+// are XOR-permuted by the row index so both the row-wise 16-byte writes and the
+// column-wise 8-byte reads are free of bank conflicts.
+__device__ __forceinline__ int xpos2(int row, int col) {  // in float2 units
+  return 16 * row + 2 * ((col >> 1) ^ (row & 7)) + (col & 1);
 }
 
-// Butterfly rotate + quantise. One CTA per row, blockDim = 32 * ceil(K/512): thread t
-// loads chunk t (16 consecutive elements), 16 threads per 256-group, 2 groups per warp.
-// The digit-2/3 stages run on the transposed chunk after a warp-local shared exchange.
+// Quantise a pair of unscaled butterfly sums S (rotated value v = S/16, exact) with
+// scale = max(fl(fl(max|v|)/127), 1e-30): code = clamp(rint(fl(v / scale)), -128, 127),
+// the same result as slimdit/int8.py:51.
+// Fast path: t = S * r16 with r16 = fl(1/(16*scale)); |t - fl(v/scale)| <= 1.5*2^-23*|t| <
+// 2.3e-5 for |t| <= 128, so rint(t) is rint(fl(v/scale)) unless t lies within 2^-13 of a
+// half-integer; those set `slow` and the caller redoes the pair with the IEEE division
+// (about 2.4e-4 of random elements). rint(t) is taken with the 1.5*2^23 magic constant,
+// whose float bit pattern then holds the code in its low byte. Rows whose maximum is tiny
+// (S/16 could be subnormal) always take the exact path.
+// Returns the two codes packed into the low 16 bits (lane x in bits 0-7).
+__device__ __forceinline__ uint32_t quant_pair(float2 S, float2 r16x2, float scale, bool& slow) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const float2 t = mul2(S, r16x2);
+  const float2 x = add2(t, make_float2(kMagic, kMagic));
+  const float2 r = add2(x, make_float2(-kMagic, -kMagic));
+  const float2 d = add2(t, make_float2(-r.x, -r.y));
+  slow |= fabsf(d.x) > 0.5f - 1.220703125e-4f;
+  slow |= fabsf(d.y) > 0.5f - 1.220703125e-4f;
+  (void)scale;
+  return __byte_perm(__float_as_uint(x.x), __float_as_uint(x.y), 0x0040);
+}
+
+// Butterfly rotate + quantise with packed pairs, persistent over rows. A row of G groups is
+// split into G2 = ceil(G/2) group pairs (g, g + G2); 16 threads per pair, thread (p, r)
+// owns chunk r (16 consecutive elements) of both groups and carries them as the two lanes
+// of float2 registers through all four radix-4 stages. Rows are staged into shared memory by
+// double-buffered bulk copies. One block barrier per row (partial maxima double-buffered).
 template <int DT>
-__global__ void __launch_bounds__(1024) bfly_rotate_quant_kernel(const void* __restrict__ x,
+__global__ void __launch_bounds__(512) bfly2_rotate_quant_kernel(const void* __restrict__ x,
                                                                  int64_t rows, int K,
                                                                  int8_t* __restrict__ q_out,
                                                                  float* __restrict__ scale_out,
                                                                  float* __restrict__ rot_out) {
-  extern __shared__ __align__(16) float smem_f[];
-  float* red = smem_f;                  // 32 floats
-  float* xbuf = smem_f + 32;            // per warp: 2 groups * kGroupPad floats
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  constexpr int kEsz = DT == kF32 ? 4 : 2;
+  const uint32_t row_bytes = static_cast<uint32_t>(K) * kEsz;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);                 // 2 mbarriers
+  float* red = reinterpret_cast<float*>(smem_raw + 16);                  // 2 x 32 partial maxima
+  unsigned char* rowbuf = smem_raw + 272;                                // 2 staged rows
+  float2* xbuf = reinterpret_cast<float2*>(rowbuf + 2 * static_cast<size_t>(row_bytes));
   const int t = threadIdx.x;
   const int warp = t >> 5, lane = t & 31;
-  const int gl = lane >> 4;             // group within the warp
-  const int r = lane & 15;              // chunk within the group
-  const int nchunks = K >> 4;
-  const bool active = t < nchunks;
-  float* gbuf = xbuf + (warp * 2 + gl) * kGroupPad;
-  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-    const int64_t base = row * static_cast<int64_t>(K) + 16 * t;
-    float v[16];
-    if (active) {
-      if (DT == kBF16) {
-        const uint4* p = reinterpret_cast<const uint4*>(static_cast<const unsigned short*>(x) + base);
-        const uint4 u0 = __ldg(p), u1 = __ldg(p + 1);
-        const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+  const int G = K >> 8;
+  const int G2 = (G + 1) >> 1;
+  const int p = t >> 4;                 // group pair
+  const int r = t & 15;                 // chunk within the group
+  const bool act_a = p < G2;
+  const bool act_b = p + G2 < G;
+  float2* gbuf = xbuf + (warp * 2 + ((lane >> 4) & 1)) * 256;
+  const int nw = (blockDim.x + 31) >> 5;
+  const unsigned char* src = static_cast<const unsigned char*>(x);
+
+  if (t == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  int64_t row = blockIdx.x;
+  uint32_t pending = 0, pending_parity = 0;
+  if (t == 0) {
+    for (int b = 0; b < 2; ++b) {
+      const int64_t rb = row + b * static_cast<int64_t>(gridDim.x);
+      if (rb < rows) {
+        mbar_arrive_expect_tx(&bar[b], row_bytes);
+        bulk_load(rowbuf + b * row_bytes, src + rb * row_bytes, row_bytes, &bar[b]);
+        pending |= 1u << b;
+      }
+    }
+  }
+  for (int it = 0; row < rows; row += gridDim.x, ++it) {
+    const int b = it & 1;
+    const bool ok = mbar_wait(&bar[b], (it >> 1) & 1, kErrWaitTimeoutProducer);
+    if (ok && t == 0) pending &= ~(1u << b);
+    if (__syncthreads_or(!ok)) break;  // a staged row never arrived: stop (error recorded)
+    const unsigned char* stage = rowbuf + b * row_bytes;
+    const int ea = (p * 256 + 16 * r);            // element offset of chunk a in the row
+    const int eb = ea + G2 * 256;                 // chunk b
+    float2 v[16];
+    if (act_a) {
+      float fa[16], fb[16];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          v[2 * e] = __uint_as_float(w[e] << 16);
-          v[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+      for (int h = 0; h < 2; ++h) {
+        const int e0 = h == 0 ? ea : eb;
+        float* f = h == 0 ? fa : fb;
+        if (h == 1 && !act_b) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) f[i] = 0.0f;
+          continue;
         }
-      } else if (DT == kF32) {
-        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + base);
+        if (DT == kF32) {
+          const float4* q4 = reinterpret_cast<const float4*>(stage + 4 * e0);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float4 f = __ldg(p + e);
-          v[4 * e] = f.x; v[4 * e + 1] = f.y; v[4 * e + 2] = f.z; v[4 * e + 3] = f.w;
-        }
-      } else {
-        const uint4* p = reinterpret_cast<const uint4*>(static_cast<const __half*>(x) + base);
-        const uint4 u0 = __ldg(p), u1 = __ldg(p + 1);
-        const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+          for (int e = 0; e < 4; ++e) {
+            const float4 g = q4[e];
+            f[4 * e] = g.x; f[4 * e + 1] = g.y; f[4 * e + 2] = g.z; f[4 * e + 3] = g.w;
+          }
+        } else {
+          const uint4* q4 = reinterpret_cast<const uint4*>(stage + 2 * e0);
+          const uint4 u0 = q4[0], u1 = q4[1];
+          const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const __half2 h = *reinterpret_cast<const __half2*>(&w[e]);
-          const float2 f = __half22float2(h);
-          v[2 * e] = f.x; v[2 * e + 1] = f.y;
+          for (int e = 0; e < 8; ++e) {
+            if (DT == kBF16) {
+              f[2 * e] = __uint_as_float(w[e] << 16);
+              f[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+            } else {
+              const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+              f[2 * e] = hf.x; f[2 * e + 1] = hf.y;
+            }
+          }
         }
       }
-      bfly16(v);  // digits 0, 1
 #pragma unroll
-      for (int i = 0; i < 16; i += 4)
-        *reinterpret_cast<float4*>(gbuf + xpos(r, i)) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      for (int i = 0; i < 16; ++i) v[i] = make_float2(fa[i], fb[i]);
+      bfly16x2(v);  // digits 0, 1
+#pragma unroll
+      for (int i = 0; i < 16; i += 2)
+        *reinterpret_cast<float4*>(gbuf + xpos2(r, i)) = make_float4(v[i].x, v[i].y, v[i + 1].x, v[i + 1].y);
     }
     __syncwarp();
-    // transposed: this thread now owns column i' = r of its group, rows r' = 0..15
-    if (active) {
-#pragma unroll
-      for (int rr = 0; rr < 16; ++rr) v[rr] = gbuf[xpos(rr, r)];
-      bfly16(v);  // digits 2, 3 (rr = 4*d3 + d2)
-    }
     float amax = 0.0f;
+    if (act_a) {
 #pragma unroll
-    for (int rr = 0; rr < 16; ++rr) {
-      v[rr] *= 0.0625f;
-      amax = fmaxf(amax, fabsf(v[rr]));
+      for (int rr = 0; rr < 16; ++rr) v[rr] = gbuf[xpos2(rr, r)];
+      bfly16x2(v);  // digits 2, 3; lanes hold the unscaled sums S = 16 * rotated
+#pragma unroll
+      for (int rr = 0; rr < 16; ++rr) amax = fmaxf(amax, fmaxf(fabsf(v[rr].x), fabsf(v[rr].y)));
     }
-    if (!active) amax = 0.0f;
-    const float m = block_max(amax, red);
-    const float scale = row_scale_from_absmax(m);
+    // row maximum: one redux per warp, one block barrier, every warp finishes the reduction
+    float* redp = red + 32 * b;
+    const unsigned wmax = __reduce_max_sync(0xffffffffu, __float_as_uint(amax));
+    if (lane == 0) redp[warp] = __uint_as_float(wmax);
+    __syncthreads();
+    const float amax_s =
+        __uint_as_float(__reduce_max_sync(0xffffffffu, lane < nw ? __float_as_uint(redp[lane]) : 0u));
+    // every thread has read this row's stage: refill the buffer with the row after next
+    if (t == 0) {
+      const int64_t rn = row + 2 * static_cast<int64_t>(gridDim.x);
+      if (rn < rows) {
+        mbar_arrive_expect_tx(&bar[b], row_bytes);
+        bulk_load(rowbuf + b * row_bytes, src + rn * row_bytes, row_bytes, &bar[b]);
+        pending |= 1u << b;
+        pending_parity = (pending_parity & ~(1u << b)) | ((((it + 2) >> 1) & 1u) << b);
+      }
+    }
+    const float scale = row_scale_from_absmax(__fmul_rn(amax_s, 0.0625f));
+    const float r16 = __frcp_rn(__fmul_rn(16.0f, scale));
+    const bool tiny_row = amax_s < 8.271806125530277e-25f;  // 2^-80
     if (t == 0) scale_out[row] = scale;
+    const int64_t rbase = row * static_cast<int64_t>(K);
     if (rot_out != nullptr) {
       __syncwarp();
-      if (active) {
+      if (act_a) {
+        const float2 s16 = make_float2(0.0625f, 0.0625f);
 #pragma unroll
-        for (int rr = 0; rr < 16; ++rr) gbuf[xpos(rr, r)] = v[rr];
+        for (int rr = 0; rr < 16; ++rr) gbuf[xpos2(rr, r)] = mul2(v[rr], s16);
       }
       __syncwarp();
-      if (active) {
-        float* o = rot_out + base;
+      if (act_a) {
 #pragma unroll
-        for (int i = 0; i < 16; i += 4)
-          *reinterpret_cast<float4*>(o + i) = *reinterpret_cast<const float4*>(gbuf + xpos(r, i));
+        for (int i = 0; i < 16; i += 2) {
+          const float4 w4 = *reinterpret_cast<const float4*>(gbuf + xpos2(r, i));
+          *reinterpret_cast<float2*>(rot_out + rbase + ea + i) = make_float2(w4.x, w4.z);
+          if (act_b) *reinterpret_cast<float2*>(rot_out + rbase + eb + i) = make_float2(w4.y, w4.w);
+        }
       }
     }
-    // codes: transpose back through shared memory as bytes, then one 16-byte store.
+    // codes: pairs packed to 16 bits, transposed back through shared memory, de-interleaved
     __syncwarp();
-    int8_t* cbuf = reinterpret_cast<int8_t*>(gbuf);
-    if (active) {
+    uint16_t* cbuf = reinterpret_cast<uint16_t*>(gbuf);
+    if (act_a) {
+      bool slow = tiny_row;
+      uint32_t c2[16];
+      const float2 r2 = make_float2(r16, r16);
 #pragma unroll
-      for (int rr = 0; rr < 16; ++rr) cbuf[16 * rr + r] = quant_code(v[rr], scale);
+      for (int rr = 0; rr < 16; ++rr) c2[rr] = quant_pair(v[rr], r2, scale, slow);
+      if (slow) {
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr) {
+          const int8_t ca = quant_code(__fmul_rn(v[rr].x, 0.0625f), scale);
+          const int8_t cb = quant_code(__fmul_rn(v[rr].y, 0.0625f), scale);
+          c2[rr] = (static_cast<uint32_t>(static_cast<uint8_t>(cb)) << 8) | static_cast<uint8_t>(ca);
+        }
+      }
+#pragma unroll
+      for (int rr = 0; rr < 16; ++rr) cbuf[16 * rr + r] = static_cast<uint16_t>(c2[rr]);
     }
     __syncwarp();
-    if (active) {
-      const uint4 c = *reinterpret_cast<const uint4*>(cbuf + 16 * r);
-      *reinterpret_cast<uint4*>(q_out + base) = c;
+    if (act_a) {
+      const uint4* c4 = reinterpret_cast<const uint4*>(cbuf + 16 * r);
+      const uint4 u0 = c4[0], u1 = c4[1];  // 16 (a, b) byte pairs of chunk r
+      uint4 oa, ob;
+      oa.x = __byte_perm(u0.x, u0.y, 0x6420); ob.x = __byte_perm(u0.x, u0.y, 0x7531);
+      oa.y = __byte_perm(u0.z, u0.w, 0x6420); ob.y = __byte_perm(u0.z, u0.w, 0x7531);
+      oa.z = __byte_perm(u1.x, u1.y, 0x6420); ob.z = __byte_perm(u1.x, u1.y, 0x7531);
+      oa.w = __byte_perm(u1.z, u1.w, 0x6420); ob.w = __byte_perm(u1.z, u1.w, 0x7531);
+      *reinterpret_cast<uint4*>(q_out + rbase + ea) = oa;
+      if (act_b) *reinterpret_cast<uint4*>(q_out + rbase + eb) = ob;
     }
     __syncwarp();
+  }
+  if (t == 0) {
+    for (int b = 0; b < 2; ++b)
+      if (pending & (1u << b)) mbar_wait(&bar[b], (pending_parity >> b) & 1u, kErrWaitTimeoutDrain);
   }
 }
 
@@ -457,25 +583,31 @@ cudaError_t launch_ref_dequant(const int8_t* q, const float* scale, int64_t rows
   return launch_ref<kF32, true, 0>(q, scale, rows, K, out, nullptr, nullptr, st);
 }
 
-size_t bfly_smem_bytes(int K) {
-  const int threads = ((K >> 4) + 31) / 32 * 32;
-  return (32 + static_cast<size_t>(threads / 32) * 2 * kGroupPad) * sizeof(float);
+size_t bfly_smem_bytes(int K, int dtype) {
+  const int g2 = ((K >> 8) + 1) >> 1;
+  const int threads = (g2 + 1) / 2 * 32;
+  const size_t esz = dtype == kF32 ? 4 : 2;
+  return 272 + 2 * esz * static_cast<size_t>(K) + static_cast<size_t>(threads / 32) * 2 * 256 * sizeof(float2);
 }
 
 cudaError_t launch_bfly_rotate_quant(const void* x, int dtype, int64_t rows, int K, int8_t* q,
                                      float* scale, float* rot_out, cudaStream_t st) {
-  const int threads = ((K >> 4) + 31) / 32 * 32;
-  const size_t smem = bfly_smem_bytes(K);
-  const int per_sm = 2048 / threads > 0 ? 2048 / threads : 1;
-  const int grid = grid_for_rows(rows, per_sm * 4);
+  const int g2 = ((K >> 8) + 1) >> 1;
+  const int threads = (g2 + 1) / 2 * 32;
+  const size_t smem = bfly_smem_bytes(K, dtype);
   void (*fn)(const void*, int64_t, int, int8_t*, float*, float*) =
-      dtype == kBF16 ? bfly_rotate_quant_kernel<kBF16>
-                     : (dtype == kF32 ? bfly_rotate_quant_kernel<kF32> : bfly_rotate_quant_kernel<kF16>);
+      dtype == kBF16 ? bfly2_rotate_quant_kernel<kBF16>
+                     : (dtype == kF32 ? bfly2_rotate_quant_kernel<kF32> : bfly2_rotate_quant_kernel<kF16>);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
+  int per_sm = 1;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  const int grid = grid_for_rows(rows, per_sm);
   fn<<<grid, threads, smem, st>>>(x, rows, K, q, scale, rot_out);
   return cudaGetLastError();
 }
