@@ -81,6 +81,63 @@ __device__ __forceinline__ float bf16_round(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));
 }
 
+// One accumulator tile row-slice: this thread's row m (TMEM lane), 256 columns from n_base,
+// read 32 columns at a time; scale/bias(/GELU) in fp32, bf16 stores, optional int32 copy.
+// All 32 lanes of the warp must call it (tcgen05.ld is warp-collective).
+__device__ __forceinline__ void epilogue_rows(const GemmI8Params& p, uint32_t tbase, int64_t m, bool row_ok,
+                                              float sam, int64_t n_base) {
+  const __nv_bfloat16* bias = static_cast<const __nv_bfloat16*>(p.bias);
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tbase + c * 32, r);
+    tmem_ld_wait();
+    const int64_t n0 = n_base + c * 32;
+    if (row_ok) {
+      if (p.acc_dbg != nullptr) {
+        int32_t* dst = p.acc_dbg + m * p.N + n0;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          if (n0 + j < p.N)
+            *reinterpret_cast<int4*>(dst + j) = make_int4(static_cast<int>(r[j]), static_cast<int>(r[j + 1]),
+                                                          static_cast<int>(r[j + 2]), static_cast<int>(r[j + 3]));
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        if (n0 + j >= p.N) break;
+        const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j));
+        const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j + 4));
+        const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (bias != nullptr) {
+          const uint4 bu = __ldg(reinterpret_cast<const uint4*>(bias + n0 + j));
+          const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            bv[2 * e] = __uint_as_float(bw[e] << 16);
+            bv[2 * e + 1] = __uint_as_float(bw[e] & 0xffff0000u);
+          }
+        }
+        float y[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float acc = static_cast<float>(static_cast<int>(r[j + e]));
+          y[e] = __fmaf_rn(acc, sam * sv[e], bv[e]);
+          if (p.epilogue == kEpiGeluTanh) y[e] = gelu_tanh(bf16_round(y[e]));
+        }
+        uint4 o;
+        o.x = pack_bf16x2(y[0], y[1]);
+        o.y = pack_bf16x2(y[2], y[3]);
+        o.z = pack_bf16x2(y[4], y[5]);
+        o.w = pack_bf16x2(y[6], y[7]);
+        *reinterpret_cast<uint4*>(out + m * p.ldo + n0 + j) = o;
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_i8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                const GemmI8Params p, int tiles_m, int tiles_n) {
@@ -203,8 +260,6 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
     const int row = quarter * 32 + lane;
     int as = 0;
     uint32_t aphase = 0;
-    const __nv_bfloat16* bias = static_cast<const __nv_bfloat16*>(p.bias);
-    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
     for (int64_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       bool ok = mbar_wait(&sh.tfull[as], aphase, kErrWaitTimeoutEpilogue);
       ok = __all_sync(0xffffffffu, ok) && !sh.abort;
@@ -220,54 +275,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
       const float sam = row_ok ? __ldg(p.sa + m) : 0.0f;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(as * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + c * 32, r);
-        tmem_ld_wait();
-        const int64_t n0 = static_cast<int64_t>(tn) * BN + c * 32;
-        if (row_ok) {
-          if (p.acc_dbg != nullptr) {
-            int32_t* dst = p.acc_dbg + m * p.N + n0;
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              if (n0 + j < p.N)
-                *reinterpret_cast<int4*>(dst + j) = make_int4(static_cast<int>(r[j]), static_cast<int>(r[j + 1]),
-                                                              static_cast<int>(r[j + 2]), static_cast<int>(r[j + 3]));
-            }
-          }
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            if (n0 + j >= p.N) break;
-            const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j));
-            const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j + 4));
-            const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-            float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            if (bias != nullptr) {
-              const uint4 bu = __ldg(reinterpret_cast<const uint4*>(bias + n0 + j));
-              const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                bv[2 * e] = __uint_as_float(bw[e] << 16);
-                bv[2 * e + 1] = __uint_as_float(bw[e] & 0xffff0000u);
-              }
-            }
-            float y[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float acc = static_cast<float>(static_cast<int>(r[j + e]));
-              y[e] = __fmaf_rn(acc, sam * sv[e], bv[e]);
-              if (p.epilogue == kEpiGeluTanh) y[e] = gelu_tanh(bf16_round(y[e]));
-            }
-            uint4 o;
-            o.x = pack_bf16x2(y[0], y[1]);
-            o.y = pack_bf16x2(y[2], y[3]);
-            o.z = pack_bf16x2(y[4], y[5]);
-            o.w = pack_bf16x2(y[6], y[7]);
-            *reinterpret_cast<uint4*>(out + m * p.ldo + n0 + j) = o;
-          }
-        }
-      }
+      epilogue_rows(p, tbase, m, row_ok, sam, static_cast<int64_t>(tn) * BN);
       tc_fence_before();
       mbar_arrive(&sh.tempty[as]);
       as ^= 1;
@@ -282,6 +290,215 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
+
+// ---------------------------------------------------------------- CTA-pair (2-SM) variant
+// A cluster of two CTAs on two SMs computes 256 x 256 output tiles with
+// tcgen05.mma.cta_group::2 (M = 256: 128 rows in each CTA; B split along N: each CTA loads
+// 128 of the tile's 256 weight rows, the pair's MMA reads both halves). Per SM and K-block
+// that is 16 KB of A + 16 KB of B instead of 16 + 32 KB, so the L2->SM feed per MMA drops by a
+// third, and the 32 KB stages allow a 6-deep ring. Protocol:
+//   * each CTA's producer waits on its own empty barrier and loads its halves; both CTAs'
+//     loads complete on CTA 0's full barrier (cp.async.bulk.tensor .cta_group::2), which CTA
+//     0's producer arms for 2 x 32 KB;
+//   * one lane of CTA 0 issues the MMAs and commits to the empty / accumulator-full barriers
+//     of both CTAs (one commit per CTA, no multicast);
+//   * every epilogue thread of both CTAs arrives on CTA 0's accumulator-empty barrier (256).
+namespace pair {
+constexpr int BNH = 128;  // weight rows per CTA
+constexpr int STAGES = 6;
+constexpr int A_BYTES = BM * BK;
+constexpr int B_BYTES = BNH * BK;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int GROUP_M2 = 16;  // 256-row tiles per raster group
+constexpr uint32_t IDESC2 = idesc_i8(2 * BM, BN);
+
+struct SharedP {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  volatile int abort;
+};
+constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + sizeof(SharedP) + 64;
+
+__device__ __forceinline__ void tile_coords2(int64_t t, int tiles_m, int tiles_n, int& tm, int& tn) {
+  const int64_t per_group = static_cast<int64_t>(GROUP_M2) * tiles_n;
+  const int64_t g = t / per_group;
+  const int first_m = static_cast<int>(g * GROUP_M2);
+  const int gm = min(tiles_m - first_m, GROUP_M2);
+  const int local = static_cast<int>(t - g * per_group);
+  tm = first_m + local % gm;
+  tn = local / gm;
+}
+
+// tiles_m counts 256-row tiles, tiles_n 256-column tiles.
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                    const GemmI8Params p, int tiles_m, int tiles_n) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  SharedP& sh = *reinterpret_cast<SharedP*>(smem + STAGES * STAGE_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int64_t pair_id = blockIdx.x >> 1;
+  const int64_t npairs = gridDim.x >> 1;
+  const int64_t total_tiles = static_cast<int64_t>(tiles_m) * tiles_n;
+  const int num_kb = static_cast<int>((p.K + BK - 1) / BK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sh.tfull[a], 1);
+      mbar_init(&sh.tempty[a], 2 * 128);
+    }
+    mbar_init(&sh.drain, 1);
+    sh.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&sh.tmem_base, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers are initialised before any remote arrive or load
+  tc_fence_after();
+  const uint32_t tmem_base = sh.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tma_a);
+      tma_prefetch_desc(&tma_b);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, last_parity = 0;
+      for (int64_t t = pair_id; t < total_tiles && !sh.abort; t += npairs) {
+        int tm, tn;
+        tile_coords2(t, tiles_m, tiles_n, tm, tn);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&sh.empty[stage], phase ^ 1, kErrWaitTimeoutProducer)) {
+            sh.abort = 1;
+            break;
+          }
+          if (sh.abort) break;
+          const uint32_t full0 = mapa_shared(smem_u32(&sh.full[stage]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&sh.full[stage], 2 * STAGE_BYTES);
+          tma_load_2d_pair(sA + stage * A_BYTES, &tma_a, full0, kb * BK, tm * (2 * BM) + static_cast<int>(rank) * BM);
+          tma_load_2d_pair(sB + stage * B_BYTES, &tma_b, full0, kb * BK, tn * BN + static_cast<int>(rank) * BNH);
+          issued |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Loads must land before the CTA may exit. CTA 0 watches its full barriers; CTA 1's
+      // loads are consumed (and their stages released to its empty barriers) by the MMAs.
+      for (int s = 0; s < STAGES; ++s) {
+        if (!(issued & (1u << s))) continue;
+        if (rank == 0) mbar_wait(&sh.full[s], (last_parity >> s) & 1, kErrWaitTimeoutDrain);
+        else mbar_wait(&sh.empty[s], (last_parity >> s) & 1, kErrWaitTimeoutDrain);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int as = 0;
+      uint32_t aphase = 0;
+      bool issued_any = false;
+      for (int64_t t = pair_id; t < total_tiles && !sh.abort; t += npairs) {
+        if (!mbar_wait(&sh.tempty[as], aphase ^ 1, kErrWaitTimeoutMma)) {
+          sh.abort = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(as * BN);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&sh.full[stage], phase, kErrWaitTimeoutMma) || sh.abort) {
+            sh.abort = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / MMA_K; ++kk) {
+            mma_i8_pair(d, smem_desc_sw128(a0 + kk * MMA_K), smem_desc_sw128(b0 + kk * MMA_K), IDESC2,
+                        (kb | kk) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          const uint32_t e = smem_u32(&sh.empty[stage]);
+          mma_commit_pair(mapa_shared(e, 0));
+          mma_commit_pair(mapa_shared(e, 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        const uint32_t f = smem_u32(&sh.tfull[as]);
+        mma_commit_pair(mapa_shared(f, 0));
+        mma_commit_pair(mapa_shared(f, 1));
+        as ^= 1;
+        if (as == 0) aphase ^= 1;
+      }
+      if (issued_any) {
+        mma_commit_pair(mapa_shared(smem_u32(&sh.drain), 0));
+        mbar_wait(&sh.drain, 0, kErrWaitTimeoutDrain);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    int as = 0;
+    uint32_t aphase = 0;
+    for (int64_t t = pair_id; t < total_tiles; t += npairs) {
+      bool ok = mbar_wait(&sh.tfull[as], aphase, kErrWaitTimeoutEpilogue);
+      ok = __all_sync(0xffffffffu, ok) && !sh.abort;
+      if (!ok) {
+        sh.abort = 1;
+        break;
+      }
+      tc_fence_after();
+      int tm, tn;
+      tile_coords2(t, tiles_m, tiles_n, tm, tn);
+      const int64_t m = static_cast<int64_t>(tm) * (2 * BM) + static_cast<int64_t>(rank) * BM + row;
+      const bool row_ok = m < p.M;
+      const float sam = row_ok ? __ldg(p.sa + m) : 0.0f;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(as * BN);
+      epilogue_rows(p, tbase, m, row_ok, sam, static_cast<int64_t>(tn) * BN);
+      tc_fence_before();
+      mbar_arrive_cluster(mapa_shared(smem_u32(&sh.tempty[as]), 0));
+      as ^= 1;
+      if (as == 0) aphase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's MMAs, loads and remote arrives are finished
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+}  // namespace pair
 
 }  // namespace gi8
 
@@ -318,22 +535,55 @@ static bool make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int
 }
 
 cudaError_t launch_gemm_i8(const GemmI8Params& p, cudaStream_t st) {
-  CUtensorMap ma, mb;
-  if (!make_kmajor_map(&ma, p.a, p.M, p.K, gi8::BM)) return cudaErrorInvalidValue;
-  if (!make_kmajor_map(&mb, p.b, p.N, p.K, gi8::BN)) return cudaErrorInvalidValue;
-  const int tiles_m = static_cast<int>((p.M + gi8::BM - 1) / gi8::BM);
-  const int tiles_n = static_cast<int>((p.N + gi8::BN - 1) / gi8::BN);
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const bool use_pair = p.M > gi8::BM;
+  CUtensorMap ma, mb;
+  if (!make_kmajor_map(&ma, p.a, p.M, p.K, gi8::BM)) return cudaErrorInvalidValue;
+  if (!make_kmajor_map(&mb, p.b, p.N, p.K, use_pair ? gi8::pair::BNH : gi8::BN)) return cudaErrorInvalidValue;
+  const int tiles_n = static_cast<int>((p.N + gi8::BN - 1) / gi8::BN);
+  if (use_pair) {
+    const int tiles_m = static_cast<int>((p.M + 2 * gi8::BM - 1) / (2 * gi8::BM));
+    static bool attr_set[64] = {false};
+    if (dev < 64 && !attr_set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(gi8::pair::gemm_i8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(gi8::pair::SMEM_BYTES));
+      if (e != cudaSuccess) return e;
+      attr_set[dev] = true;
+    }
+    static int max_pairs[64] = {0};
+    if (dev < 64 && max_pairs[dev] == 0) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * (sms / 2));
+      cfg.blockDim = dim3(gi8::THREADS);
+      cfg.dynamicSmemBytes = gi8::pair::SMEM_BYTES;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 2;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, gi8::pair::gemm_i8_pair_kernel, &cfg) != cudaSuccess || clusters < 1)
+        clusters = sms / 2;
+      max_pairs[dev] = clusters;
+    }
+    const int64_t total = static_cast<int64_t>(tiles_m) * tiles_n;
+    const int pairs = static_cast<int>(total < max_pairs[dev] ? total : max_pairs[dev]);
+    gi8::pair::gemm_i8_pair_kernel<<<2 * pairs, gi8::THREADS, gi8::pair::SMEM_BYTES, st>>>(ma, mb, p, tiles_m, tiles_n);
+    return cudaGetLastError();
+  }
+  const int tiles_m = static_cast<int>((p.M + gi8::BM - 1) / gi8::BM);
   const int64_t total = static_cast<int64_t>(tiles_m) * tiles_n;
   const int grid = static_cast<int>(total < sms ? total : sms);
-  static bool attr_set[64] = {false};
-  if (dev < 64 && !attr_set[dev]) {
+  static bool attr_set1[64] = {false};
+  if (dev < 64 && !attr_set1[dev]) {
     cudaError_t e = cudaFuncSetAttribute(gi8::gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(gi8::SMEM_BYTES));
     if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+    attr_set1[dev] = true;
   }
   gi8::gemm_i8_kernel<<<grid, gi8::THREADS, gi8::SMEM_BYTES, st>>>(ma, mb, p, tiles_m, tiles_n);
   return cudaGetLastError();
