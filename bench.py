@@ -279,7 +279,51 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
     out["ffn_pair"] = {"workload": "115200 tokens, 5120 -> 13824 (GELU-tanh, requant) -> 5120, int8 convrot",
                        "tokens_per_gpu": m, "ms_per_step": round(ms, 4), "value": round(ops_total / (ms * 1e-3) / 1e12, 1),
                        "unit": "TOPS", "scaling": "strong", "steps": steps}
-    del x, xq, sx, h, hq, sh, y, qu, qd
+    del xq, sx, h, hq, sh, y, qu, qd
+    torch.cuda.empty_cache()
+
+    # ---- config 3: NVFP4 up-proj (rotate + per-token NVFP4 of x, block-scaled FP4 GEMM)
+    wu = (torch.randn((FFN_F, FFN_H), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    pw, pws, pwg = ops.nvfp4_pack(wu)
+    del wu
+    pad = (m + 127) // 128 * 128
+    xq4 = torch.empty((m, FFN_H // 2), dtype=torch.uint8, device=dev)
+    xsf4 = torch.empty((pad, FFN_H // 16), dtype=torch.uint8, device=dev)
+    xs4 = torch.empty((m,), dtype=torch.float32, device=dev)
+    h4 = torch.empty((m, FFN_F), dtype=torch.bfloat16, device=dev)
+
+    def fp4_quant():
+        _native.check(lib.slim_quant_nvfp4_act(x.data_ptr(), _native.BF16, m, FFN_H, 1, xq4.data_ptr(), xsf4.data_ptr(),
+                                               xs4.data_ptr(), sp))
+
+    def fp4_gemm():
+        _native.check(lib.slim_gemm_nvfp4(xq4.data_ptr(), xsf4.data_ptr(), xs4.data_ptr(), pw.data_ptr(),
+                                          pws.data_ptr(), pwg.data_ptr(), None, h4.data_ptr(), None, m, FFN_F, FFN_H,
+                                          _native.EPI_SCALE_BIAS, sp))
+
+    for _ in range(3):
+        fp4_quant()
+        fp4_gemm()
+    torch.cuda.synchronize(dev)
+    barrier()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    gq = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    evs[0].record(stream)
+    for i in range(steps):
+        fp4_quant()
+        gq[i].record(stream)
+        fp4_gemm()
+        evs[i + 1].record(stream)
+    torch.cuda.synchronize(dev)
+    ms = reduce_max(evs[0].elapsed_time(evs[-1]) / steps)
+    gemm_ms = reduce_max(sum(gq[i].elapsed_time(evs[i + 1]) for i in range(steps)) / steps)
+    ops_up = 2.0 * FFN_TOKENS * FFN_H * FFN_F
+    out["nvfp4_up_proj"] = {
+        "workload": "115200 tokens x 5120 -> 13824, x rotated + per-token NVFP4, W NVFP4 (E2M1 + UE4M3/16 + fp32)",
+        "tokens_per_gpu": m, "ms_per_step": round(ms, 4), "gemm_ms": round(gemm_ms, 4),
+        "value": round(ops_up / (ms * 1e-3) / 1e12, 1), "gemm_value": round(ops_up / (gemm_ms * 1e-3) / 1e12, 1),
+        "unit": "TOPS", "scaling": "strong", "steps": steps}
+    del x, xq4, xsf4, xs4, h4, pw, pws, pwg
     torch.cuda.empty_cache()
 
     # ---- config 4: converter kernels (rotate + per-row INT8 of each block linear)
@@ -307,7 +351,33 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
             "workload": "40 blocks x {qkv 15360x5120, out 5120x5120, fc1 13824x5120, fc2 5120x13824} bf16 -> int8 + scales",
             "ms_total": round(ms, 3), "value": round(total / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
             "algorithmic_bytes": total, "scaling": "strong"}
-    del ws, qs, ss
+    # NVFP4 weights: per-tensor amax pass + pack (bf16 read twice, 0.5 + 1/16 B written per element)
+    del qs, ss
+    pq = [torch.empty((r, k // 2), dtype=torch.uint8, device=dev) for r, k in CONVERT_SHAPES]
+    psf = [torch.empty((r, k // 16), dtype=torch.uint8, device=dev) for r, k in CONVERT_SHAPES]
+    pts = torch.empty((len(CONVERT_SHAPES),), dtype=torch.float32, device=dev)
+
+    def block_fp4():
+        for i, (w, (r, k)) in enumerate(zip(ws, CONVERT_SHAPES)):
+            _native.check(lib.slim_nvfp4_pack(w.data_ptr(), _native.BF16, r, k, pq[i].data_ptr(), psf[i].data_ptr(),
+                                              pts[i:].data_ptr(), sp))
+
+    block_fp4()
+    torch.cuda.synchronize(dev)
+    barrier()
+    a.record(stream)
+    for _ in range(my_blocks):
+        block_fp4()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = reduce_max(a.elapsed_time(b))
+    elems = CONVERT_BLOCKS * sum(r * k for r, k in CONVERT_SHAPES)
+    fp4_bytes = elems * (2 + 0.5 + 1 / 16)
+    out["convert_nvfp4"] = {
+        "workload": "40 blocks x {qkv, out, fc1, fc2} bf16 -> NVFP4 (per-tensor amax pass + pack)",
+        "ms_total": round(ms, 3), "value": round(fp4_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+        "algorithmic_bytes": int(fp4_bytes), "bytes_moved_two_pass": int(fp4_bytes + 2 * elems), "scaling": "strong"}
+    del ws, pq, psf, pts
     torch.cuda.empty_cache()
     return out
 
@@ -445,7 +515,7 @@ def run_ours(args) -> int:
             peak_src = f"2 x fallback bf16 {regime}"
         gemm_tops = OPS_PER_STEP / (gemm_ms * 1e-3) / 1e12
         traffic = None
-        prof = ROOT / "profiles" / "gemm_i8_qkv_32768x15360x5120.md"
+        prof = ROOT / "profiles" / "gemm_i8_pair_qkv_32768x15360x5120.md"
         if prof.exists():
             for ln in prof.read_text().splitlines():
                 if ln.startswith("dram_bytes_per_launch:"):
@@ -458,7 +528,7 @@ def run_ours(args) -> int:
                                    "int8 GEMM vs W [15360,5120] -> bf16 [32768,15360] (+bias)",
                        "M": M, "N": N, "K": K, "tokens_per_gpu": M, "parallelism": f"token rows x{world}, no collective",
                        "l2": "inputs+outputs 1.5 GB per step > 126 MB L2 (no flush needed)"},
-            "roofline": {"bound": "tensor", "kernel": "gemm_i8_kernel (tcgen05 kind::i8)",
+            "roofline": {"bound": "tensor", "kernel": "gemm_i8_pair_kernel (tcgen05 kind::i8, cta_group::2)",
                          "achieved": round(gemm_tops, 2), "peak": round(peak, 1), "unit": "TOPS",
                          "frac": round(gemm_tops / peak, 4), "peak_source": peak_src,
                          "frac_of_nominal_4500": round(gemm_tops / NOMINAL_I8_TOPS, 4), "traffic": traffic,
@@ -470,9 +540,15 @@ def run_ours(args) -> int:
         }
         if secondary is not None:
             peak_hbm = float(peaks.get("hbm_gbs", 6650.0))
-            for key in ("convert_reference_order", "convert_butterfly_order"):
-                secondary[key]["frac_of_measured_hbm"] = round(secondary[key]["value"] / peak_hbm, 4)
+            for key in ("convert_reference_order", "convert_butterfly_order", "convert_nvfp4"):
+                secondary[key]["frac_of_measured_hbm"] = round(secondary[key]["value"] / (world * peak_hbm), 4)
             secondary["ffn_pair"]["frac_of_i8_peak"] = round(secondary["ffn_pair"]["value"] / (world * peak), 4)
+            # dense FP4 (kind::mxf4nvf4) issues at four times kind::f16's rate
+            fp4_peak = 2.0 * peak
+            nv = secondary["nvfp4_up_proj"]
+            nv["fp4_peak"] = round(fp4_peak, 1)
+            nv["frac_of_fp4_peak"] = round(nv["value"] / (world * fp4_peak), 4)
+            nv["gemm_frac_of_fp4_peak"] = round(nv["gemm_value"] / (world * fp4_peak), 4)
             line["secondary"] = secondary
         if e2e is not None:
             line["e2e"] = {"value": round(world * OPS_PER_STEP / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TOPS",

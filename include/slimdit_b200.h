@@ -121,6 +121,59 @@ int slim_int8_linear_noalloc(const void* x, int x_dtype, const int8_t* qw, const
                              const void* bias, void* out, int64_t M, int64_t N, int64_t K,
                              int group, int epilogue, void* stream);
 
+/* ---------------------------------------------------------------- NVFP4
+ * Format of slimdit/nvfp4.py:3-8: E2M1 codes packed two per byte (element 2i in the low
+ * nibble), one UE4M3 scale per 16 consecutive elements along K stored in the cuBLAS 128x4
+ * tiled layout (scale (r, c) of a [R, C = K/16] matrix at byte
+ * ((r/128)*(C/4) + c/4)*512 + (r%32)*16 + ((r%128)/32)*4 + c%4), and an fp32 global scale
+ * gs = amax / (448 * 6). Block scale = e4m3(min(fl(fl(block_amax / 6) / gs), 448)); codes =
+ * E2M1 round-half-even of fl(x / fl(gs * block_scale)). All sizes need K % 64 == 0 and
+ * K <= 16384. */
+
+/* Weight packing with one global scale per tensor. Replaces
+ * slimdit.nvfp4.quantize_nvfp4_weight (slimdit/nvfp4.py:72-87; the reference delegates the
+ * arithmetic to comfy_kitchen's TensorCoreNVFP4Layout.quantize).
+ * w: [rows, K] of `dtype`, rows % 128 == 0; q: uint8 [rows, K/2]; block_scale: uint8
+ * [rows, K/16]; tensor_scale: one fp32 in device memory (weight_scale_2). */
+int slim_nvfp4_pack(const void* w, int dtype, int64_t rows, int64_t K, uint8_t* q,
+                    uint8_t* block_scale, float* tensor_scale, void* stream);
+
+/* Activation quantisation for the NVFP4 linear: one global scale per token row
+ * (row_scale fp32 [rows]), optionally after the group-256 Hadamard rotation in the
+ * butterfly order (rotate != 0; K % 256 == 0). q: uint8 [rows, K/2]; block_scale: uint8
+ * [round_up(rows, 128), K/16] (padding rows get zero scales). The input side of the NVFP4
+ * runtime linear that consumes slimdit/nvfp4.py's format. */
+int slim_quant_nvfp4_act(const void* x, int dtype, int64_t rows, int64_t K, int rotate,
+                         uint8_t* q, uint8_t* block_scale, float* row_scale, void* stream);
+
+/* out[r, k] = code * fl(scale * block_scale) in fp32 (scale[0] for the tensor, or
+ * scale[r] when per_row). out may be NULL when err is given; err (fp64[2] in device
+ * memory, accumulated into, not cleared) receives sum (out - x)^2 and sum x^2 against the
+ * original x of x_dtype: the round-trip error of slimdit.nvfp4.quantize_nvfp4_with_error
+ * (slimdit/nvfp4.py:90-105). */
+int slim_nvfp4_dequant(const uint8_t* q, const uint8_t* block_scale, const float* scale,
+                       int per_row, int64_t rows, int64_t K, float* out, const void* x,
+                       int x_dtype, double* err, void* stream);
+
+/* out[m,n] = bf16(acc * (a_scale[m] * b_scale[0]) + bias[n]) (optionally GELU-tanh),
+ * acc = sum_k (a[m,k] * a_sf) * (b[n,k] * b_sf) accumulated in fp32 by the block-scaled
+ * tensor cores (tcgen05 kind::mxf4nvf4). a: [M, K/2], a_sf: [round_up(M,128), K/16];
+ * b: [N, K/2] with N % 128 == 0, b_sf: [N, K/16]; acc_dbg: fp32 [M, N] or NULL.
+ * The FP4 GEMM of the NVFP4 runtime linear (the reference measures comfy_kitchen's,
+ * docs/DEV_NOTES.md:204-206). */
+int slim_gemm_nvfp4(const uint8_t* a, const uint8_t* a_sf, const float* a_scale,
+                    const uint8_t* b, const uint8_t* b_sf, const float* b_scale,
+                    const void* bias, void* out, float* acc_dbg, int64_t M, int64_t N,
+                    int64_t K, int epilogue, void* stream);
+
+/* The NVFP4 linear: slim_quant_nvfp4_act of x [M,K] into the caller's workspaces
+ * (xq_ws uint8 [M, K/2], xsf_ws uint8 [round_up(M,128), K/16], xs_ws fp32 [M]), then
+ * slim_gemm_nvfp4 against the packed weight (qw, w_sf, w_scale). */
+int slim_nvfp4_linear(const void* x, int x_dtype, const uint8_t* qw, const uint8_t* w_sf,
+                      const float* w_scale, const void* bias, void* out, uint8_t* xq_ws,
+                      uint8_t* xsf_ws, float* xs_ws, int64_t M, int64_t N, int64_t K,
+                      int rotate, int epilogue, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -12,7 +12,10 @@ inputs (tests/synthetic.py):
   * per-token activation quantisation with the reference's own math (rotate + int8.py:49-51);
   * SHA-256 of the full config-0 weight conversion (W [5120, 5120]);
   * the descriptor blob, and the bytes (SHA-256 + header) of reference convert() runs on a
-    2-block synthetic official checkpoint (full, and with block_limit=0).
+    2-block synthetic official checkpoint (full, and with block_limit=0);
+  * the NVFP4 host contract of slimdit/nvfp4.py that needs no comfy_kitchen: descriptor
+    bytes, quantized_shapes results and errors, and convert.output_manifest(quant="nvfp4")
+    on the same checkpoint.
 The GPU box has no reference tree: tests read only these fixtures.
 """
 
@@ -47,6 +50,31 @@ CONVERT_CASE = {"n_blocks": 2, "hidden": 512, "ffn": 1024, "time_hidden": 64, "s
 
 def sha256(b: bytes) -> str:
     return hashlib.sha256(b).hexdigest()
+
+
+def nvfp4_contract(src_dir) -> dict:
+    from slimdit import mapping, nvfp4
+    from slimdit import convert as ref_convert
+    from slimdit.safetensors_io import ShardSet
+
+    shapes = {}
+    for rows, cols in [(128, 64), (13824, 5120), (5120, 13824), (15360, 5120), (100, 64), (128, 48), (128, 80)]:
+        try:
+            shapes[f"{rows}x{cols}"] = [list(s) for s in nvfp4.quantized_shapes(rows, cols)]
+        except ValueError as err:
+            shapes[f"{rows}x{cols}"] = f"ValueError: {err}"
+    src = ShardSet(src_dir)
+    ops = mapping.build_plan(src.manifest.keys())
+    manifest = ref_convert.output_manifest(ops, src, 8, 65, None, quant="nvfp4")
+    return {
+        "descriptor": nvfp4.NVFP4_DESCRIPTOR,
+        "blob": [int(b) for b in nvfp4.comfy_quant_blob()],
+        "block": nvfp4.NVFP4_BLOCK,
+        "blob_len": nvfp4.BLOB_LEN,
+        "shapes": shapes,
+        "available_without_comfy_kitchen": bool(nvfp4.nvfp4_available()),
+        "output_manifest": [[n, d, list(s)] for n, d, s in manifest],
+    }
 
 
 def main(argv=None) -> int:
@@ -117,6 +145,7 @@ def main(argv=None) -> int:
         raw0 = out0.read_bytes()
         meta["convert_block0"] = {"case": CONVERT_CASE, "rank": 8, "grid": 65, "block_limit": 0,
                                   "sha256_file": sha256(raw0), "size": len(raw0)}
+        meta["nvfp4"] = nvfp4_contract(src)
     (HERE / "golden.json").write_text(json.dumps(meta, indent=1, sort_keys=True))
     print("wrote", HERE / "rotation_quant.npz", HERE / "golden.json")
     return 0

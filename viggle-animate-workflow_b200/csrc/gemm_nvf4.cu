@@ -1,0 +1,316 @@
+// Block-scaled FP4 (NVFP4) GEMM on the sm_100a tensor cores (tcgen05.mma kind::mxf4nvf4,
+// scale_vec::4X) with a dequantising epilogue:
+//
+//   out[m, n] = bf16( acc[m, n] * (sa[m] * sb) + bias[n] ),
+//   acc[m, n] = sum_k (ea[m,k] * fa[m, k/16]) * (eb[n,k] * fb[n, k/16])   (fp32, tensor core)
+//
+// ea/eb are E2M1 values (packed two per byte, element 2i in the low nibble), fa/fb their
+// UE4M3 block scales in the cuBLAS 128x4 tiled layout, sa the activation's per-token global
+// scale and sb the weight's per-tensor global scale (slimdit/nvfp4.py:3-8: weight,
+// weight_scale, weight_scale_2). This is the runtime side of an NVFP4 linear.
+//
+// Structure (one CTA per SM, persistent over 128 x 256 output tiles, K-blocks of 256 FP4):
+//   warp 0      producer: TMA tiles of A (128 x 128 B) and B (256 x 128 B), 128-byte swizzle,
+//               plus bulk copies of the k-block's scale atoms (2 KB of A, 2 x 2 KB of B),
+//               into a 4-stage ring guarded by full/empty mbarriers.
+//   warp 1      allocates 512 TMEM columns: a 256-column fp32 accumulator and, per stage, 48
+//               scale columns (A: 4 MMAs x 4, B: 4 MMAs x 8). One lane copies the stage's
+//               scale atoms to TMEM (tcgen05.cp 32x128b.warpx4) and issues 4 MMAs
+//               (M=128, N=256, K=64) per stage; a stage's TMEM scale columns are reused only
+//               after its empty barrier has completed, i.e. after the MMAs that read them.
+//   warps 2..9  epilogue: the 8 warps read the accumulator (lane quarter warp%4, column half
+//               (warp-2)/4) into registers, release it to the next tile's MMAs at once, then
+//               scale/bias(/GELU) in fp32 and store bf16.
+// Every mbarrier wait is bounded; on a timeout the kernel records an error, drains its
+// copies and MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "slim_kernels.h"
+#include "slim_ptx.cuh"
+
+namespace slim {
+namespace gf4 {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BKB = 128;                  // bytes of packed FP4 per row per k-block (256 elements)
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BKB;         // 16 KB
+constexpr int B_BYTES = BN * BKB;         // 32 KB
+constexpr int ATOM = 512;                 // one 128-row x 4-scale tile
+constexpr int SFA_BYTES = 4 * ATOM;       // 4 atoms per k-block
+constexpr int SFB_BYTES = 8 * ATOM;       // 2 row tiles x 4 atoms
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+constexpr int MMA_KB = 32;                // bytes of one MMA's K (64 FP4 elements)
+constexpr int THREADS = 320;
+constexpr int TMEM_COLS = 512;
+constexpr int SF_COL0 = 256;
+constexpr int SF_COLS = 48;
+constexpr int GROUP_M = 16;
+constexpr uint32_t IDESC = idesc_nvf4(BM, BN);
+
+struct Shared {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull;
+  uint64_t tempty;
+  uint64_t drain;
+  uint32_t tmem_base;
+  volatile int abort;
+};
+
+constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + sizeof(Shared) + 64;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+static_assert(SF_COL0 + STAGES * SF_COLS <= TMEM_COLS, "TMEM budget");
+
+__device__ __forceinline__ void tile_coords(int64_t t, int tiles_m, int tiles_n, int& tm, int& tn) {
+  const int64_t per_group = static_cast<int64_t>(GROUP_M) * tiles_n;
+  const int64_t g = t / per_group;
+  const int first_m = static_cast<int>(g * GROUP_M);
+  const int gm = min(tiles_m - first_m, GROUP_M);
+  const int local = static_cast<int>(t - g * per_group);
+  tm = first_m + local % gm;
+  tn = local / gm;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_nvf4_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                 const GemmNvf4Params p, int tiles_m, int tiles_n) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * A_BYTES;
+  uint8_t* sFA = sB + STAGES * B_BYTES;
+  uint8_t* sFB = sFA + STAGES * SFA_BYTES;
+  Shared& sh = *reinterpret_cast<Shared*>(smem + STAGES * STAGE_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t total_tiles = static_cast<int64_t>(tiles_m) * tiles_n;
+  const int64_t ctiles = p.K / 64;                       // scale atoms per 128-row tile
+  const int num_kb = static_cast<int>((p.K + 255) / 256);
+  const int64_t n_rowtiles = p.N / 128;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    mbar_init(&sh.tfull, 1);
+    mbar_init(&sh.tempty, 256);
+    mbar_init(&sh.drain, 1);
+    sh.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sh.tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = sh.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tma_a);
+      tma_prefetch_desc(&tma_b);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, last_parity = 0;
+      for (int64_t t = blockIdx.x; t < total_tiles && !sh.abort; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, tiles_m, tiles_n, tm, tn);
+        const bool rb1 = 2 * static_cast<int64_t>(tn) + 1 < n_rowtiles;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          const int64_t atom0 = 4 * static_cast<int64_t>(kb);
+          const uint32_t nat = static_cast<uint32_t>(ctiles - atom0 < 4 ? ctiles - atom0 : 4);
+          if (!mbar_wait(&sh.empty[stage], phase ^ 1, kErrWaitTimeoutProducer)) {
+            sh.abort = 1;
+            break;
+          }
+          if (sh.abort) break;
+          const uint32_t sfb = nat * ATOM;
+          mbar_arrive_expect_tx(&sh.full[stage], A_BYTES + B_BYTES + sfb * (rb1 ? 3u : 2u));
+          tma_load_2d(sA + stage * A_BYTES, &tma_a, &sh.full[stage], kb * BKB, tm * BM);
+          tma_load_2d(sB + stage * B_BYTES, &tma_b, &sh.full[stage], kb * BKB, tn * BN);
+          bulk_load(sFA + stage * SFA_BYTES, p.sfa + (static_cast<int64_t>(tm) * ctiles + atom0) * ATOM, sfb,
+                    &sh.full[stage]);
+          bulk_load(sFB + stage * SFB_BYTES, p.sfb + (2 * static_cast<int64_t>(tn) * ctiles + atom0) * ATOM, sfb,
+                    &sh.full[stage]);
+          if (rb1)
+            bulk_load(sFB + stage * SFB_BYTES + 4 * ATOM,
+                      p.sfb + ((2 * static_cast<int64_t>(tn) + 1) * ctiles + atom0) * ATOM, sfb, &sh.full[stage]);
+          issued |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      for (int s = 0; s < STAGES; ++s)
+        if (issued & (1u << s)) mbar_wait(&sh.full[s], (last_parity >> s) & 1, kErrWaitTimeoutDrain);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t aphase = 0;
+      bool issued_any = false;
+      for (int64_t t = blockIdx.x; t < total_tiles && !sh.abort; t += gridDim.x) {
+        if (!mbar_wait(&sh.tempty, aphase ^ 1, kErrWaitTimeoutMma)) {
+          sh.abort = 1;
+          break;
+        }
+        tc_fence_after();
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          const int64_t atom0 = 4 * static_cast<int64_t>(kb);
+          const int nat = static_cast<int>(ctiles - atom0 < 4 ? ctiles - atom0 : 4);
+          if (!mbar_wait(&sh.full[stage], phase, kErrWaitTimeoutMma) || sh.abort) {
+            sh.abort = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sf_t = tmem_base + static_cast<uint32_t>(SF_COL0 + stage * SF_COLS);
+          const uint32_t fa = smem_u32(sFA + stage * SFA_BYTES);
+          const uint32_t fb = smem_u32(sFB + stage * SFB_BYTES);
+          for (int kk = 0; kk < nat; ++kk) {
+            tmem_cp_32x128b_warpx4(sf_t + kk * 4, smem_desc_sf(fa + kk * ATOM));
+            tmem_cp_32x128b_warpx4(sf_t + 16 + kk * 8, smem_desc_sf(fb + kk * ATOM));
+            tmem_cp_32x128b_warpx4(sf_t + 16 + kk * 8 + 4, smem_desc_sf(fb + (4 + kk) * ATOM));
+          }
+          const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+          for (int kk = 0; kk < nat; ++kk) {
+            mma_nvf4(tmem_base, smem_desc_sw128(a0 + kk * MMA_KB), smem_desc_sw128(b0 + kk * MMA_KB), IDESC,
+                     sf_t + kk * 4, sf_t + 16 + kk * 8, (kb | kk) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          mma_commit(&sh.empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&sh.tfull);
+        aphase ^= 1;
+      }
+      if (issued_any) {
+        mma_commit(&sh.drain);
+        mbar_wait(&sh.drain, 0, kErrWaitTimeoutDrain);
+      }
+    }
+    __syncwarp();
+  } else {
+    // epilogue warps 2..9
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    const __nv_bfloat16* bias = static_cast<const __nv_bfloat16*>(p.bias);
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+    const float sb = __ldg(p.sb);
+    uint32_t aphase = 0;
+    for (int64_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      bool ok = mbar_wait(&sh.tfull, aphase, kErrWaitTimeoutEpilogue);
+      ok = __all_sync(0xffffffffu, ok) && !sh.abort;
+      if (!ok) {
+        sh.abort = 1;
+        break;
+      }
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, tm, tn);
+      const int64_t m = static_cast<int64_t>(tm) * BM + row;
+      const bool row_ok = m < p.M;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(half * 128);
+      uint32_t r[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tbase + c * 32, r[c]);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&sh.tempty);  // the accumulator is in registers: the next tile may start
+      aphase ^= 1;
+      if (row_ok) {
+        const float alpha = __fmul_rn(__ldg(p.sa + m), sb);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int64_t n0 = static_cast<int64_t>(tn) * BN + half * 128 + c * 32;
+          if (n0 >= p.N) break;
+          if (p.acc_dbg != nullptr) {
+            float* dst = p.acc_dbg + m * p.N + n0;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[c][j]), __uint_as_float(r[c][j + 1]),
+                                                                __uint_as_float(r[c][j + 2]), __uint_as_float(r[c][j + 3]));
+          }
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (bias != nullptr) {
+              const uint4 bu = __ldg(reinterpret_cast<const uint4*>(bias + n0 + j));
+              const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                bv[2 * e] = __uint_as_float(bw[e] << 16);
+                bv[2 * e + 1] = __uint_as_float(bw[e] & 0xffff0000u);
+              }
+            }
+            float y[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              y[e] = __fmaf_rn(__uint_as_float(r[c][j + e]), alpha, bv[e]);
+              if (p.epilogue == kEpiGeluTanh) y[e] = gi8::gelu_tanh(gi8::bf16_round(y[e]));
+            }
+            uint4 o;
+            o.x = gi8::pack_bf16x2(y[0], y[1]);
+            o.y = gi8::pack_bf16x2(y[2], y[3]);
+            o.z = gi8::pack_bf16x2(y[4], y[5]);
+            o.w = gi8::pack_bf16x2(y[6], y[7]);
+            *reinterpret_cast<uint4*>(out + m * p.ldo + n0 + j) = o;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace gf4
+
+cudaError_t launch_gemm_nvf4(const GemmNvf4Params& p, cudaStream_t st) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  CUtensorMap ma, mb;
+  if (!make_kmajor_map(&ma, p.a, p.M, p.K / 2, gf4::BM)) return cudaErrorInvalidValue;
+  if (!make_kmajor_map(&mb, p.b, p.N, p.K / 2, gf4::BN)) return cudaErrorInvalidValue;
+  const int tiles_m = static_cast<int>((p.M + gf4::BM - 1) / gf4::BM);
+  const int tiles_n = static_cast<int>((p.N + gf4::BN - 1) / gf4::BN);
+  const int64_t total = static_cast<int64_t>(tiles_m) * tiles_n;
+  const int grid = static_cast<int>(total < sms ? total : sms);
+  static bool attr_set[64] = {false};
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gf4::gemm_nvf4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(gf4::SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  gf4::gemm_nvf4_kernel<<<grid, gf4::THREADS, gf4::SMEM_BYTES, st>>>(ma, mb, p, tiles_m, tiles_n);
+  return cudaGetLastError();
+}
+
+}  // namespace slim

@@ -1,0 +1,391 @@
+// NVFP4 quantisation: E2M1 codes in 16-element blocks along K with UE4M3 block scales and an
+// fp32 global scale, the format of slimdit/nvfp4.py (weight, weight_scale, weight_scale_2;
+// slimdit/nvfp4.py:3-8, docs/DEV_NOTES.md:59-71).
+//
+// The recipe (the reference delegates it to comfy_kitchen, slimdit/nvfp4.py:44-51,72-87):
+//   global  gs = fl32(amax / 2688)                       (2688 = 448 * 6)
+//   block   sf = e4m3_rne(min(fl32(fl32(block_amax / 6) / gs), 448))
+//   element v  = fl32(x / fl32(gs * float(sf)))  (0 when that product is 0)
+//           code = E2M1 round-half-even of v, saturating at 6, sign bit kept (0b1000 for
+//                  negative values that round to zero)
+// Every division is IEEE (div.rn); the E4M3 rounding is the hardware cvt.rn.satfinite.
+// Packing: element 2i in the low nibble of byte i (the order the tensor cores read).
+// Block scales are written in the cuBLAS 128x4 tiled layout: scale (r, c) of a matrix with
+// C = K/16 scale columns lives at ((r/128)*(C/4) + c/4)*512 + (r%32)*16 + ((r%128)/32)*4 + c%4.
+//
+// Weights use one global scale per tensor (amax pass first); activations use one per token
+// row (per-row amax inside the quantiser), optionally after the group-256 Hadamard rotation
+// in the butterfly order of the INT8 path (bit-identical rotated values).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "slim_kernels.h"
+#include "slim_ptx.cuh"
+
+namespace slim {
+namespace nvf4q {
+
+__device__ __forceinline__ int64_t blocked_offset(int64_t row, int c, int ctiles) {
+  return ((row >> 7) * ctiles + (c >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4 + (c & 3);
+}
+
+// Exact value of a UE4M3 byte (0..0x7E).
+__device__ __forceinline__ float e4m3_value(uint32_t b) {
+  const uint32_t e = (b >> 3) & 15u, m = b & 7u;
+  return e == 0 ? static_cast<float>(m) * 0.001953125f : __uint_as_float(((e + 120u) << 23) | (m << 20));
+}
+
+__device__ __forceinline__ uint32_t e4m3_rne(float s) {
+  return static_cast<uint32_t>(__nv_cvt_float_to_fp8(s, __NV_SATFINITE, __NV_E4M3));
+}
+
+// E2M1 code of v (round half to even on |v|, saturating at 6; sign in bit 3).
+__device__ __forceinline__ uint32_t e2m1_code(float v) {
+  const float a = fabsf(v);
+  const uint32_t c = static_cast<uint32_t>(a > 0.25f) + static_cast<uint32_t>(a >= 0.75f) +
+                     static_cast<uint32_t>(a > 1.25f) + static_cast<uint32_t>(a >= 1.75f) +
+                     static_cast<uint32_t>(a > 2.5f) + static_cast<uint32_t>(a >= 3.5f) +
+                     static_cast<uint32_t>(a > 5.0f);
+  return c | ((__float_as_uint(v) >> 28) & 8u);
+}
+
+// One 16-element block -> 8 packed bytes and its scale byte.
+__device__ __forceinline__ void quant_block16(const float (&v)[16], float gs, uint2& packed, uint32_t& sfb) {
+  float bm = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) bm = fmaxf(bm, fabsf(v[i]));
+  sfb = 0;
+  if (gs > 0.0f) {
+    const float s2 = fminf(__fdiv_rn(__fdiv_rn(bm, 6.0f), gs), 448.0f);
+    sfb = e4m3_rne(s2);
+  }
+  const float total = __fmul_rn(gs, e4m3_value(sfb));
+  uint32_t w[2] = {0u, 0u};
+  if (total != 0.0f) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) w[i >> 3] |= e2m1_code(__fdiv_rn(v[i], total)) << (4 * (i & 7));
+  }
+  packed = make_uint2(w[0], w[1]);
+}
+
+template <int DT>
+__device__ __forceinline__ void load16(const void* x, int64_t e0, float (&f)[16]) {
+  if (DT == kF32) {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + e0);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float4 g = __ldg(p + e);
+      f[4 * e] = g.x; f[4 * e + 1] = g.y; f[4 * e + 2] = g.z; f[4 * e + 3] = g.w;
+    }
+  } else {
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const unsigned short*>(x) + e0);
+    const uint4 u0 = __ldg(p), u1 = __ldg(p + 1);
+    const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (DT == kBF16) {
+        f[2 * e] = __uint_as_float(w[e] << 16);
+        f[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+      } else {
+        const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+        f[2 * e] = h.x; f[2 * e + 1] = h.y;
+      }
+    }
+  }
+}
+
+// Radix-4 butterfly step b_i = ((a0 + a1) + (a2 + a3)) - 2*a_{3-i}, each operation rounded
+// to fp32 (the product 2*a is exact, so the fma rounds once, like the subtraction).
+__device__ __forceinline__ void bfly4(float& a0, float& a1, float& a2, float& a3) {
+  const float s = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+  const float b0 = __fmaf_rn(-2.0f, a3, s), b1 = __fmaf_rn(-2.0f, a2, s);
+  const float b2 = __fmaf_rn(-2.0f, a1, s), b3 = __fmaf_rn(-2.0f, a0, s);
+  a0 = b0; a1 = b1; a2 = b2; a3 = b3;
+}
+
+// Base-4 digits 0 and 1 of a 16-element chunk.
+__device__ __forceinline__ void bfly16(float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) bfly4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+#pragma unroll
+  for (int m = 0; m < 4; ++m) bfly4(v[m], v[4 + m], v[8 + m], v[12 + m]);
+}
+
+// Exchange buffer of one 256-element group (16 chunks x 16 floats); 16-byte slots of a row
+// are XOR-permuted by (row >> 1) & 3, so row-wise float4 writes and column-wise scalar reads
+// are free of bank conflicts (groups are 272 floats apart to separate half-warps' banks).
+__device__ __forceinline__ int xpos(int row, int col) {
+  return 16 * row + 4 * ((col >> 2) ^ ((row >> 1) & 3)) + (col & 3);
+}
+
+// One CTA per row (persistent over rows), thread c owns 16-element block c of the row.
+// Rows in [rows, rows_pad) only get zero scale bytes (padding of the last 128-row tile).
+// ROW_SCALE: global scale per row (written to row_scale); else per tensor from *amax_in.
+template <int DT, bool ROT, bool ROW_SCALE>
+__global__ void __launch_bounds__(1024) nvfp4_quant_kernel(const void* __restrict__ x, int64_t rows,
+                                                           int64_t rows_pad, int K,
+                                                           const float* __restrict__ amax_in,
+                                                           uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
+                                                           float* __restrict__ row_scale) {
+  extern __shared__ __align__(16) float xch[];
+  __shared__ float red[2][32];
+  const int t = threadIdx.x;
+  const int nb = K >> 4;
+  const int ctiles = K >> 6;
+  const bool act = t < nb;
+  const int lane = t & 31, warp = t >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  float gs_tensor = 0.0f;
+  if (!ROW_SCALE) gs_tensor = __fdiv_rn(__ldg(amax_in), 2688.0f);
+  float* g = xch + (t >> 4) * 272;
+  const int r = t & 15;
+  int it = 0;
+  for (int64_t row = blockIdx.x; row < rows_pad; row += gridDim.x, ++it) {
+    if (row >= rows) {
+      if (act) sf[blocked_offset(row, t, ctiles)] = 0;
+      continue;
+    }
+    float v[16];
+    if (act) {
+      load16<DT>(x, row * K + 16 * t, v);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+    }
+    if (ROT) {
+      bfly16(v);  // digits 0, 1 (within the chunk)
+      if (act) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(g + xpos(r, i)) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      }
+      __syncwarp();
+      if (act) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = g[xpos(i, r)];
+      }
+      bfly16(v);  // digits 2, 3 (across the group's chunks)
+      __syncwarp();
+      if (act) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) g[xpos(i, r)] = v[i];
+      }
+      __syncwarp();
+      if (act) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 w = *reinterpret_cast<const float4*>(g + xpos(r, i));
+          v[i] = __fmul_rn(w.x, 0.0625f); v[i + 1] = __fmul_rn(w.y, 0.0625f);
+          v[i + 2] = __fmul_rn(w.z, 0.0625f); v[i + 3] = __fmul_rn(w.w, 0.0625f);
+        }
+      }
+      __syncwarp();
+    }
+    float gs = gs_tensor;
+    if (ROW_SCALE) {
+      float am = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) am = fmaxf(am, fabsf(v[i]));
+      const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(am));
+      if (lane == 0) red[it & 1][warp] = __uint_as_float(wm);
+      __syncthreads();
+      const float rm = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < nw ? __float_as_uint(red[it & 1][lane]) : 0u));
+      gs = __fdiv_rn(rm, 2688.0f);
+      if (t == 0) row_scale[row] = gs;
+    }
+    if (act) {
+      uint2 packed;
+      uint32_t sfb;
+      quant_block16(v, gs, packed, sfb);
+      *reinterpret_cast<uint2*>(q + row * (K >> 1) + 8 * t) = packed;
+      sf[blocked_offset(row, t, ctiles)] = static_cast<uint8_t>(sfb);
+    }
+  }
+}
+
+// Per-tensor absmax of n elements (n % 8 == 0 for 16-bit types, % 4 for fp32) into *out
+// (as the bits of a non-negative float, combined with atomicMax; *out must start at 0).
+template <int DT>
+__global__ void __launch_bounds__(256) nvfp4_amax_kernel(const void* __restrict__ x, int64_t n,
+                                                         unsigned int* __restrict__ out) {
+  float m = 0.0f;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if (DT == kF32) {
+    const float4* p = static_cast<const float4*>(x);
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n / 4; i += stride) {
+      const float4 g = __ldg(p + i);
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(g.x), fabsf(g.y)), fmaxf(fabsf(g.z), fabsf(g.w))));
+    }
+  } else {
+    const uint4* p = static_cast<const uint4*>(x);
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n / 8; i += stride) {
+      const uint4 u = __ldg(p + i);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float lo, hi;
+        if (DT == kBF16) {
+          lo = __uint_as_float(w[e] << 16);
+          hi = __uint_as_float(w[e] & 0xffff0000u);
+        } else {
+          const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+          lo = h.x; hi = h.y;
+        }
+        m = fmaxf(m, fmaxf(fabsf(lo), fabsf(hi)));
+      }
+    }
+  }
+  const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+  if ((threadIdx.x & 31) == 0 && wm != 0u) atomicMax(out, wm);
+}
+
+// *s = fl32(*s / 2688): the per-tensor amax becomes the global scale.
+__global__ void nvfp4_finalize_scale_kernel(float* s) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) *s = __fdiv_rn(*s, 2688.0f);
+}
+
+// out[r, k] = code * fl32(scale_r * sf) (scale per tensor, or per row when per_row), fp32.
+// Optionally accumulates sum (out - x)^2 and sum x^2 over the matrix in fp64 (err[0], err[1])
+// for the converter's error report (x of dtype DT, may be null).
+template <int DT>
+__global__ void __launch_bounds__(256) nvfp4_dequant_kernel(const uint8_t* __restrict__ q,
+                                                            const uint8_t* __restrict__ sf,
+                                                            const float* __restrict__ scale, int per_row,
+                                                            int64_t rows, int K, float* __restrict__ out,
+                                                            const void* __restrict__ x, double* __restrict__ err) {
+  const int nb = K >> 4;
+  const int ctiles = K >> 6;
+  const int64_t total = rows * nb;
+  double e2 = 0.0, x2 = 0.0;
+  for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < total;
+       b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = b / nb;
+    const int c = static_cast<int>(b - row * nb);
+    const float s = __ldg(scale + (per_row ? row : 0));
+    const float bs = __fmul_rn(s, e4m3_value(sf[blocked_offset(row, c, ctiles)]));
+    const uint2 pk = *reinterpret_cast<const uint2*>(q + row * (K >> 1) + 8 * c);
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t code = ((i < 8 ? pk.x : pk.y) >> (4 * (i & 7))) & 15u;
+      const uint32_t mag = code & 7u;
+      const float a = mag < 4 ? 0.5f * static_cast<float>(mag) : (mag == 4 ? 2.0f : (mag == 5 ? 3.0f : (mag == 6 ? 4.0f : 6.0f)));
+      v[i] = __fmul_rn((code & 8u) ? -a : a, bs);
+    }
+    if (out != nullptr) {
+      float4* o = reinterpret_cast<float4*>(out + row * K + 16 * c);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+    }
+    if (err != nullptr) {
+      float xf[16];
+      load16<DT>(x, row * K + 16 * c, xf);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const double d = static_cast<double>(v[i]) - static_cast<double>(xf[i]);
+        e2 += d * d;
+        x2 += static_cast<double>(xf[i]) * static_cast<double>(xf[i]);
+      }
+    }
+  }
+  if (err != nullptr) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      e2 += __shfl_xor_sync(0xffffffffu, e2, o);
+      x2 += __shfl_xor_sync(0xffffffffu, x2, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+      atomicAdd(err, e2);
+      atomicAdd(err + 1, x2);
+    }
+  }
+}
+
+static int sm_count() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+template <int DT, bool ROT, bool ROW_SCALE>
+static cudaError_t launch_quant_t(const void* x, int64_t rows, int64_t rows_pad, int K, const float* amax_in,
+                                  uint8_t* q, uint8_t* sf, float* row_scale, cudaStream_t st) {
+  const int threads = ((K >> 4) + 31) / 32 * 32;
+  const size_t smem = ROT ? static_cast<size_t>(threads / 16) * 272 * sizeof(float) : 0;
+  auto fn = nvfp4_quant_kernel<DT, ROT, ROW_SCALE>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  int per_sm = 1;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm;
+  const int grid = static_cast<int>(rows_pad < cap ? rows_pad : cap);
+  fn<<<grid, threads, smem, st>>>(x, rows, rows_pad, K, amax_in, q, sf, row_scale);
+  return cudaGetLastError();
+}
+
+template <bool ROT, bool ROW_SCALE>
+static cudaError_t launch_quant_dt(int dtype, const void* x, int64_t rows, int64_t rows_pad, int K,
+                                   const float* amax_in, uint8_t* q, uint8_t* sf, float* row_scale, cudaStream_t st) {
+  switch (dtype) {
+    case kF32: return launch_quant_t<kF32, ROT, ROW_SCALE>(x, rows, rows_pad, K, amax_in, q, sf, row_scale, st);
+    case kBF16: return launch_quant_t<kBF16, ROT, ROW_SCALE>(x, rows, rows_pad, K, amax_in, q, sf, row_scale, st);
+    case kF16: return launch_quant_t<kF16, ROT, ROW_SCALE>(x, rows, rows_pad, K, amax_in, q, sf, row_scale, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace nvf4q
+
+// Number of kernel launches made by the call (for the launch counter).
+cudaError_t launch_nvfp4_pack(const void* w, int dtype, int64_t rows, int K, uint8_t* q, uint8_t* sf,
+                              float* tensor_scale, int* launches, cudaStream_t st) {
+  *launches = 0;
+  cudaError_t e = cudaMemsetAsync(tensor_scale, 0, sizeof(float), st);
+  if (e != cudaSuccess) return e;
+  const int64_t n = rows * static_cast<int64_t>(K);
+  const int grid = nvf4q::sm_count() * 8;
+  unsigned int* amax = reinterpret_cast<unsigned int*>(tensor_scale);
+  switch (dtype) {
+    case kF32: nvf4q::nvfp4_amax_kernel<kF32><<<grid, 256, 0, st>>>(w, n, amax); break;
+    case kBF16: nvf4q::nvfp4_amax_kernel<kBF16><<<grid, 256, 0, st>>>(w, n, amax); break;
+    case kF16: nvf4q::nvfp4_amax_kernel<kF16><<<grid, 256, 0, st>>>(w, n, amax); break;
+    default: return cudaErrorInvalidValue;
+  }
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  ++*launches;
+  e = nvf4q::launch_quant_dt<false, false>(dtype, w, rows, rows, K, tensor_scale, q, sf, nullptr, st);
+  if (e != cudaSuccess) return e;
+  ++*launches;
+  nvf4q::nvfp4_finalize_scale_kernel<<<1, 32, 0, st>>>(tensor_scale);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  ++*launches;
+  return cudaSuccess;
+}
+
+cudaError_t launch_nvfp4_quant_rows(const void* x, int dtype, int64_t rows, int K, int rotate, uint8_t* q,
+                                    uint8_t* sf, float* row_scale, cudaStream_t st) {
+  const int64_t rows_pad = (rows + 127) / 128 * 128;
+  if (rotate) return nvf4q::launch_quant_dt<true, true>(dtype, x, rows, rows_pad, K, nullptr, q, sf, row_scale, st);
+  return nvf4q::launch_quant_dt<false, true>(dtype, x, rows, rows_pad, K, nullptr, q, sf, row_scale, st);
+}
+
+cudaError_t launch_nvfp4_dequant(const uint8_t* q, const uint8_t* sf, const float* scale, int per_row, int64_t rows,
+                                 int K, float* out, const void* x, int x_dtype, double* err, cudaStream_t st) {
+  const int grid = nvf4q::sm_count() * 8;
+  switch (x == nullptr ? kF32 : x_dtype) {
+    case kF32: nvf4q::nvfp4_dequant_kernel<kF32><<<grid, 256, 0, st>>>(q, sf, scale, per_row, rows, K, out, x, err); break;
+    case kBF16: nvf4q::nvfp4_dequant_kernel<kBF16><<<grid, 256, 0, st>>>(q, sf, scale, per_row, rows, K, out, x, err); break;
+    case kF16: nvf4q::nvfp4_dequant_kernel<kF16><<<grid, 256, 0, st>>>(q, sf, scale, per_row, rows, K, out, x, err); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace slim

@@ -42,6 +42,31 @@ struct GemmI8Params {
 };
 cudaError_t launch_gemm_i8(const GemmI8Params& p, cudaStream_t st);
 
+// nvfp4_quant.cu
+cudaError_t launch_nvfp4_pack(const void* w, int dtype, int64_t rows, int K, uint8_t* q, uint8_t* sf,
+                              float* tensor_scale, int* launches, cudaStream_t st);
+cudaError_t launch_nvfp4_quant_rows(const void* x, int dtype, int64_t rows, int K, int rotate, uint8_t* q,
+                                    uint8_t* sf, float* row_scale, cudaStream_t st);
+cudaError_t launch_nvfp4_dequant(const uint8_t* q, const uint8_t* sf, const float* scale, int per_row, int64_t rows,
+                                 int K, float* out, const void* x, int x_dtype, double* err, cudaStream_t st);
+
+// gemm_nvf4.cu
+struct GemmNvf4Params {
+  const uint8_t* a;       // [M, K/2] packed E2M1 (token rows)
+  const uint8_t* b;       // [N, K/2] packed E2M1 (output channels)
+  const uint8_t* sfa;     // UE4M3 block scales of a, tiled layout, [round_up(M,128), K/16]
+  const uint8_t* sfb;     // UE4M3 block scales of b, tiled layout, [N, K/16]
+  const float* sa;        // [M] per-token global scales
+  const float* sb;        // [1] per-tensor global scale of b
+  const void* bias;       // bf16 [N] or null
+  void* out;              // bf16 [M, N] row-major, row pitch ldo elements
+  float* acc_dbg;         // fp32 [M, N] raw accumulators or null
+  int64_t M, N, K;
+  int64_t ldo;
+  int epilogue;
+};
+cudaError_t launch_gemm_nvf4(const GemmNvf4Params& p, cudaStream_t st);
+
 // Count of kernels launched by this library since load (instrumentation for benches).
 uint64_t launch_count();
 void note_launch(uint64_t n = 1);

@@ -205,6 +205,49 @@ __host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
          | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
 }
 
+// ---------------------------------------------------------------- block-scaled FP4 (NVFP4)
+// Instruction descriptor for kind::mxf4nvf4 with scale_vec::4X: A and B E2M1 (packed two per
+// byte), K-major, UE4M3 block scales (bit 23 = 0), fp32 accumulator, scale-factor IDs 0.
+__host__ __device__ constexpr uint32_t idesc_nvf4(int m, int n) {
+  return (1u << 7)                                   // A: E2M1
+         | (1u << 10)                                // B: E2M1
+         | (static_cast<uint32_t>(n >> 3) << 17)     // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
+}
+
+// D[tmem] (+)= (A . SFA) * (B . SFB)^T over K = 64 FP4 elements (32 bytes per row): every 16
+// consecutive K elements of a row share one UE4M3 scale. sfa / sfb are the TMEM addresses of
+// the scale factors (32-lane x 4-column atoms per 128 rows, see tmem_cp_32x128b_warpx4).
+__device__ __forceinline__ void mma_nvf4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
+      : "memory");
+}
+
+// Shared memory -> TMEM copy of one 512-byte scale atom: 32 rows of 16 bytes (the 128x4 tile
+// of the cuBLAS block-scale layout, row r%32 holding rows r, r+32, r+64, r+96), written to 32
+// lanes x 4 columns and replicated into all four lane quarters. Issued by one thread;
+// ordered before the same thread's later tcgen05.mma.
+__device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Shared-memory descriptor of an unswizzled 32 x 16-byte scale atom: 8-row core matrices of
+// 128 contiguous bytes, 128 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sf(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFF) >> 4);       // start address
+  d |= static_cast<uint64_t>(128 >> 4) << 16;                // LBO (one 16-byte column: unused)
+  d |= static_cast<uint64_t>(128 >> 4) << 32;                // SBO: 8 rows * 16 B
+  d |= static_cast<uint64_t>(1) << 46;                       // descriptor version (sm_100)
+  return d;                                                  // layout: no swizzle (0)
+}
+
 // ---------------------------------------------------------------- CTA pairs (cluster of 2)
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

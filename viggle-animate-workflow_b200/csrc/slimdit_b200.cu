@@ -4,3 +4,6 @@
 #include "gemm_i8.cu"
 #include "rotate_quant.cu"
 #include "linear_noalloc.cu"
+#include "nvfp4_quant.cu"
+#include "gemm_nvf4.cu"
+#include "capi_nvfp4.cu"

@@ -189,3 +189,139 @@ def ffn_int8(x: torch.Tensor, w_up: torch.Tensor, s_up: torch.Tensor, w_down: to
     """
     h = int8_linear(x, w_up, s_up, bias=b_up, epilogue="gelu_tanh")
     return int8_linear(h, w_down, s_down, bias=b_down)
+
+
+# ---------------------------------------------------------------- NVFP4
+# Format of slimdit/nvfp4.py:3-8 (weight uint8 [N, K/2], weight_scale uint8 [N, K/16] in the
+# 128x4 tiled layout, weight_scale_2 fp32); the arithmetic runs in libslimdit_b200.so.
+
+def _rows_pad(rows: int) -> int:
+    return (rows + 127) // 128 * 128
+
+
+def nvfp4_pack(w: torch.Tensor):
+    """Per-tensor NVFP4 of a [N, K] weight (f32/bf16/f16 CUDA) -> (uint8 [N, K/2], uint8
+    [N, K/16] tiled block scales, fp32 [1] global scale), as slimdit/nvfp4.py:72-87."""
+    w = _cuda2d(w, "weight")
+    if w.dtype not in _DT:
+        raise TypeError(f"unsupported dtype {w.dtype}")
+    n, k = w.shape
+    q = torch.empty((n, k // 2), dtype=torch.uint8, device=w.device)
+    sf = torch.empty((n, k // 16), dtype=torch.uint8, device=w.device)
+    ts = torch.empty((1,), dtype=torch.float32, device=w.device)
+    with torch.cuda.device(w.device):
+        nat.check(nat.load().slim_nvfp4_pack(w.data_ptr(), _DT[w.dtype], n, k, q.data_ptr(), sf.data_ptr(),
+                                             ts.data_ptr(), _stream(w)))
+    return q, sf, ts
+
+
+def nvfp4_quantize_act(x: torch.Tensor, rotate: bool = False, out=None):
+    """Per-token NVFP4 of activations [M, K] (optionally rotated first) -> (uint8 [M, K/2],
+    uint8 [round_up(M, 128), K/16] tiled block scales, fp32 [M] row scales)."""
+    x = _cuda2d(x, "input")
+    if x.dtype not in _DT:
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    m, k = x.shape
+    if out is None:
+        q = torch.empty((m, k // 2), dtype=torch.uint8, device=x.device)
+        sf = torch.empty((_rows_pad(m), k // 16), dtype=torch.uint8, device=x.device)
+        rs = torch.empty((m,), dtype=torch.float32, device=x.device)
+    else:
+        q, sf, rs = out
+    with torch.cuda.device(x.device):
+        nat.check(nat.load().slim_quant_nvfp4_act(x.data_ptr(), _DT[x.dtype], m, k, int(bool(rotate)), q.data_ptr(),
+                                                  sf.data_ptr(), rs.data_ptr(), _stream(x)))
+    return q, sf, rs
+
+
+def nvfp4_dequantize(q: torch.Tensor, sf: torch.Tensor, scale: torch.Tensor, per_row: bool = False) -> torch.Tensor:
+    """code * (scale * block_scale) -> fp32 [rows, K]."""
+    q = _cuda2d(q, "q")
+    rows, k = q.shape[0], q.shape[1] * 2
+    scale = scale.to(device=q.device, dtype=torch.float32).contiguous().reshape(-1)
+    out = torch.empty((rows, k), dtype=torch.float32, device=q.device)
+    with torch.cuda.device(q.device):
+        nat.check(nat.load().slim_nvfp4_dequant(q.data_ptr(), sf.contiguous().data_ptr(), scale.data_ptr(),
+                                                int(bool(per_row)), rows, k, out.data_ptr(), None, 0, None,
+                                                _stream(q)))
+    return out
+
+
+def nvfp4_error(q: torch.Tensor, sf: torch.Tensor, scale: torch.Tensor, x: torch.Tensor) -> float:
+    """Relative round-trip error ||dequant - x|| / ||x|| (slimdit/nvfp4.py:98-99), fp64 sums."""
+    q = _cuda2d(q, "q")
+    x = _cuda2d(x, "x")
+    rows, k = q.shape[0], q.shape[1] * 2
+    scale = scale.to(device=q.device, dtype=torch.float32).contiguous().reshape(-1)
+    acc = torch.zeros((2,), dtype=torch.float64, device=q.device)
+    with torch.cuda.device(q.device):
+        nat.check(nat.load().slim_nvfp4_dequant(q.data_ptr(), sf.contiguous().data_ptr(), scale.data_ptr(), 0, rows, k,
+                                                None, x.data_ptr(), _DT[x.dtype], acc.data_ptr(), _stream(q)))
+    e2, x2 = acc.cpu().tolist()
+    return float((e2 / x2) ** 0.5) if x2 > 0 else 0.0
+
+
+def gemm_nvfp4(a: torch.Tensor, a_sf: torch.Tensor, a_scale: torch.Tensor, b: torch.Tensor, b_sf: torch.Tensor,
+               b_scale: torch.Tensor, bias: torch.Tensor | None = None, epilogue: str | None = None,
+               return_acc: bool = False, out: torch.Tensor | None = None):
+    """bf16(acc * a_scale[m] * b_scale + bias[n]) for NVFP4 a [M, K/2] and b [N, K/2]."""
+    a = _cuda2d(a, "a")
+    b = _cuda2d(b, "b")
+    if a.dtype != torch.uint8 or b.dtype != torch.uint8:
+        raise TypeError("a and b must be uint8 (packed E2M1)")
+    m, k = a.shape[0], a.shape[1] * 2
+    n = b.shape[0]
+    if b.shape[1] * 2 != k:
+        raise ValueError(f"K mismatch: a {tuple(a.shape)} vs b {tuple(b.shape)}")
+    if epilogue not in _EPI:
+        raise ValueError(f"epilogue must be one of {sorted(str(e) for e in _EPI)}")
+    dev = a.device
+    if a_sf.numel() < _rows_pad(m) * (k // 16) or b_sf.numel() != n * (k // 16):
+        raise ValueError("block-scale tensors have the wrong size")
+    a_scale = _vec(a_scale, m, torch.float32, dev, "a_scale")
+    b_scale = _vec(b_scale, 1, torch.float32, dev, "b_scale")
+    bias = _vec(bias, n, torch.bfloat16, dev, "bias")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    acc = torch.empty((m, n), dtype=torch.float32, device=dev) if return_acc else None
+    with torch.cuda.device(dev):
+        nat.check(nat.load().slim_gemm_nvfp4(a.data_ptr(), a_sf.contiguous().data_ptr(), a_scale.data_ptr(),
+                                             b.data_ptr(), b_sf.contiguous().data_ptr(), b_scale.data_ptr(),
+                                             _ptr(bias), out.data_ptr(), _ptr(acc), m, n, k, _EPI[epilogue],
+                                             _stream(a)))
+    return (out, acc) if return_acc else out
+
+
+def nvfp4_linear(x: torch.Tensor, qweight: torch.Tensor, block_scale: torch.Tensor, tensor_scale: torch.Tensor,
+                 bias: torch.Tensor | None = None, rotate: bool = False, epilogue: str | None = None,
+                 out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """NVFP4 linear on the checkpoint tensors of slimdit/nvfp4.py (weight, weight_scale,
+    weight_scale_2): x [..., K] is quantised per token to NVFP4 (optionally after the
+    group-256 rotation, for weights packed from rotated rows), then the block-scaled FP4 GEMM."""
+    nat.require_cuda()
+    if not x.is_cuda:
+        raise TypeError("x must be a CUDA tensor")
+    if x.dtype not in _DT:
+        raise TypeError(f"unsupported activation dtype {x.dtype}")
+    qweight = _cuda2d(qweight, "qweight")
+    k = x.shape[-1]
+    n = qweight.shape[0]
+    if qweight.shape[1] * 2 != k:
+        raise ValueError(f"in_features mismatch: x [..., {k}] vs packed weight {tuple(qweight.shape)}")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, k).contiguous()
+    m = x2.shape[0]
+    dev = x2.device
+    ts = _vec(tensor_scale, 1, torch.float32, dev, "tensor_scale")
+    b = _vec(bias, n, torch.bfloat16, dev, "bias")
+    bs = block_scale.to(dev).contiguous()
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    xq = torch.empty((m, k // 2), dtype=torch.uint8, device=dev)
+    xsf = torch.empty((_rows_pad(m), k // 16), dtype=torch.uint8, device=dev)
+    xs = torch.empty((m,), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        nat.check(nat.load().slim_nvfp4_linear(x2.data_ptr(), _DT[x2.dtype], qweight.data_ptr(), bs.data_ptr(),
+                                               ts.data_ptr(), _ptr(b), out.data_ptr(), xq.data_ptr(), xsf.data_ptr(),
+                                               xs.data_ptr(), m, n, k, int(bool(rotate)), _EPI[epilogue], _stream(x2)))
+    out = out.reshape(*lead, n)
+    return out if out_dtype == torch.bfloat16 else out.to(out_dtype)
