@@ -55,6 +55,9 @@ def parse_args(argv=None):
     ap.add_argument("--no-secondary", action="store_true", help="skip the FFN and converter measurements")
     ap.add_argument("--secondary-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU work in the cpu_baseline sample")
+    ap.add_argument("--profile-case", choices=["nvfp4"], default=None,
+                    help="run only a small case of one workload (for ncu captures; prints no bench line)")
+    ap.add_argument("--tokens", type=int, default=16384, help="token rows of the --profile-case run")
     return ap.parse_args(argv)
 
 
@@ -382,6 +385,46 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
     return out
 
 
+# ----------------------------------------------------------------------------- profiling cases
+def run_profile_case(args) -> int:
+    """A small case of the config-3 NVFP4 up-proj (x [tokens, 5120] rotated + per-token
+    NVFP4, FP4 GEMM against W [13824, 5120]): warm-up + `--steps` launches of each kernel, for
+    ncu captures that must stay a few GB. Prints a JSON line marked "profile_case"."""
+    import torch
+
+    from slimdit import _native, ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = _native.load()
+    sp = torch.cuda.current_stream(dev).cuda_stream
+    m = args.tokens
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    x = (torch.randn((m, FFN_H), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    w = (torch.randn((FFN_F, FFN_H), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    pw, pws, pwg = ops.nvfp4_pack(w)
+    xq = torch.empty((m, FFN_H // 2), dtype=torch.uint8, device=dev)
+    xsf = torch.empty(((m + 127) // 128 * 128, FFN_H // 16), dtype=torch.uint8, device=dev)
+    xs = torch.empty((m,), dtype=torch.float32, device=dev)
+    h = torch.empty((m, FFN_F), dtype=torch.bfloat16, device=dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(max(3, args.warmup) + args.steps):
+        if i == max(3, args.warmup):
+            a.record()
+        _native.check(lib.slim_quant_nvfp4_act(x.data_ptr(), _native.BF16, m, FFN_H, 1, xq.data_ptr(), xsf.data_ptr(),
+                                               xs.data_ptr(), sp))
+        _native.check(lib.slim_gemm_nvfp4(xq.data_ptr(), xsf.data_ptr(), xs.data_ptr(), pw.data_ptr(), pws.data_ptr(),
+                                          pwg.data_ptr(), None, h.data_ptr(), None, m, FFN_F, FFN_H,
+                                          _native.EPI_SCALE_BIAS, sp))
+    b.record()
+    torch.cuda.synchronize(dev)
+    assert _native.device_error() == 0
+    print(json.dumps({"profile_case": "nvfp4_up_proj", "tokens": m, "steps": args.steps,
+                      "ms_per_step": round(a.elapsed_time(b) / max(1, args.steps), 4)}))
+    return 0
+
+
 # ----------------------------------------------------------------------------- ours
 def run_ours(args) -> int:
     import torch
@@ -567,6 +610,8 @@ def main(argv=None) -> int:
     args = parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile_case:
+        return run_profile_case(args)
     return run_ours(args)
 
 

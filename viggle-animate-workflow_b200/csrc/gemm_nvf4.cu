@@ -10,17 +10,25 @@
 // weight_scale, weight_scale_2). This is the runtime side of an NVFP4 linear.
 //
 // Structure (one CTA per SM, persistent over 128 x 256 output tiles, K-blocks of 256 FP4):
-//   warp 0      producer: TMA tiles of A (128 x 128 B) and B (256 x 128 B), 128-byte swizzle,
-//               plus bulk copies of the k-block's scale atoms (2 KB of A, 2 x 2 KB of B),
-//               into a 4-stage ring guarded by full/empty mbarriers.
-//   warp 1      allocates 512 TMEM columns: a 256-column fp32 accumulator and, per stage, 48
-//               scale columns (A: 4 MMAs x 4, B: 4 MMAs x 8). One lane copies the stage's
-//               scale atoms to TMEM (tcgen05.cp 32x128b.warpx4) and issues 4 MMAs
-//               (M=128, N=256, K=64) per stage; a stage's TMEM scale columns are reused only
-//               after its empty barrier has completed, i.e. after the MMAs that read them.
-//   warps 2..9  epilogue: the 8 warps read the accumulator (lane quarter warp%4, column half
-//               (warp-2)/4) into registers, release it to the next tile's MMAs at once, then
-//               scale/bias(/GELU) in fp32 and store bf16.
+//   warp 0       producer: TMA tiles of A (128 x 128 B) and B (256 x 128 B), 128-byte swizzle,
+//                plus bulk copies of the k-block's scale atoms (2 KB of A, 2 x 2 KB of B), into
+//                a 4-stage ring guarded by full/empty mbarriers.
+//   warp 1       allocates 512 TMEM columns: a 256-column fp32 accumulator and, per stage, 48
+//                scale columns; one lane issues 4 MMAs (M=128, N=256, K=64) per stage.
+//   warps 2..5   scale loaders, one per TMEM lane quarter: each lane reads its 16-byte line of
+//                every 512-byte scale atom of the stage from shared memory and writes it to
+//                the stage's scale columns with tcgen05.st (A: 4 atoms x 4 columns, B: 8 x 4).
+//                A 128-row atom sits in 32 lanes x 4 columns, line i (rows i, i+32, i+64, i+96)
+//                in lane i of every quarter: the layout the MMA reads (the one tcgen05.cp
+//                .32x128b.warpx4 produces). Issued by these warps, the scale writes stay out of
+//                the MMA issue stream (a tcgen05.cp issued there after MMAs held back the MMAs
+//                behind it: 2.7 vs 4.1 POPS measured). A stage's scale columns are written once
+//                its full barrier completes: by then the MMAs that last read them are done,
+//                since the producer refilled the stage only after they committed. sf_full hands
+//                the columns to the MMA warp.
+//   warps 6..13  epilogue: each warp reads 128 accumulator columns of its lane quarter,
+//                scales + biases them (GELU if asked) and packs bf16 in registers, releases the
+//                accumulator to the next tile's MMAs, then stores.
 // Every mbarrier wait is bounded; on a timeout the kernel records an error, drains its
 // copies and MMAs, frees TMEM and returns.
 #include <cuda.h>
@@ -40,21 +48,24 @@ constexpr int BKB = 128;                  // bytes of packed FP4 per row per k-b
 constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BKB;         // 16 KB
 constexpr int B_BYTES = BN * BKB;         // 32 KB
-constexpr int ATOM = 512;                 // one 128-row x 4-scale tile
-constexpr int SFA_BYTES = 4 * ATOM;       // 4 atoms per k-block
-constexpr int SFB_BYTES = 8 * ATOM;       // 2 row tiles x 4 atoms
+constexpr int ATOM = 512;                 // one 128-row x 4-scale tile of the block-scale layout
+constexpr int SFA_BYTES = 4 * ATOM;       // A scales of a k-block: 4 atoms
+constexpr int SFB_BYTES = 8 * ATOM;       // B scales: 2 row tiles x 4 atoms
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
 constexpr int MMA_KB = 32;                // bytes of one MMA's K (64 FP4 elements)
-constexpr int THREADS = 320;
+constexpr int SF_WARP0 = 2;
+constexpr int EPI_WARP0 = 6;
+constexpr int THREADS = 14 * 32;
 constexpr int TMEM_COLS = 512;
 constexpr int SF_COL0 = 256;
-constexpr int SF_COLS = 48;
+constexpr int SF_COLS = 48;               // per stage: A 4 atoms x 4 columns, B 8 atoms x 4 columns
 constexpr int GROUP_M = 16;
 constexpr uint32_t IDESC = idesc_nvf4(BM, BN);
 
 struct Shared {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
+  uint64_t sf_full[STAGES];
   uint64_t tfull;
   uint64_t tempty;
   uint64_t drain;
@@ -99,6 +110,7 @@ gemm_nvf4_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&sh.full[s], 1);
       mbar_init(&sh.empty[s], 1);
+      mbar_init(&sh.sf_full[s], 4);
     }
     mbar_init(&sh.tfull, 1);
     mbar_init(&sh.tempty, 256);
@@ -128,23 +140,22 @@ gemm_nvf4_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
         const bool rb1 = 2 * static_cast<int64_t>(tn) + 1 < n_rowtiles;
         for (int kb = 0; kb < num_kb; ++kb) {
           const int64_t atom0 = 4 * static_cast<int64_t>(kb);
-          const uint32_t nat = static_cast<uint32_t>(ctiles - atom0 < 4 ? ctiles - atom0 : 4);
+          const uint32_t sfbytes = static_cast<uint32_t>(ctiles - atom0 < 4 ? ctiles - atom0 : 4) * ATOM;
           if (!mbar_wait(&sh.empty[stage], phase ^ 1, kErrWaitTimeoutProducer)) {
             sh.abort = 1;
             break;
           }
           if (sh.abort) break;
-          const uint32_t sfb = nat * ATOM;
-          mbar_arrive_expect_tx(&sh.full[stage], A_BYTES + B_BYTES + sfb * (rb1 ? 3u : 2u));
+          mbar_arrive_expect_tx(&sh.full[stage], A_BYTES + B_BYTES + sfbytes * (rb1 ? 3u : 2u));
           tma_load_2d(sA + stage * A_BYTES, &tma_a, &sh.full[stage], kb * BKB, tm * BM);
           tma_load_2d(sB + stage * B_BYTES, &tma_b, &sh.full[stage], kb * BKB, tn * BN);
-          bulk_load(sFA + stage * SFA_BYTES, p.sfa + (static_cast<int64_t>(tm) * ctiles + atom0) * ATOM, sfb,
+          bulk_load(sFA + stage * SFA_BYTES, p.sfa + (static_cast<int64_t>(tm) * ctiles + atom0) * ATOM, sfbytes,
                     &sh.full[stage]);
-          bulk_load(sFB + stage * SFB_BYTES, p.sfb + (2 * static_cast<int64_t>(tn) * ctiles + atom0) * ATOM, sfb,
+          bulk_load(sFB + stage * SFB_BYTES, p.sfb + (2 * static_cast<int64_t>(tn) * ctiles + atom0) * ATOM, sfbytes,
                     &sh.full[stage]);
           if (rb1)
             bulk_load(sFB + stage * SFB_BYTES + 4 * ATOM,
-                      p.sfb + ((2 * static_cast<int64_t>(tn) + 1) * ctiles + atom0) * ATOM, sfb, &sh.full[stage]);
+                      p.sfb + ((2 * static_cast<int64_t>(tn) + 1) * ctiles + atom0) * ATOM, sfbytes, &sh.full[stage]);
           issued |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -172,20 +183,14 @@ gemm_nvf4_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
         for (int kb = 0; kb < num_kb; ++kb) {
           const int64_t atom0 = 4 * static_cast<int64_t>(kb);
           const int nat = static_cast<int>(ctiles - atom0 < 4 ? ctiles - atom0 : 4);
-          if (!mbar_wait(&sh.full[stage], phase, kErrWaitTimeoutMma) || sh.abort) {
+          if (!mbar_wait(&sh.full[stage], phase, kErrWaitTimeoutMma) ||
+              !mbar_wait(&sh.sf_full[stage], phase, kErrWaitTimeoutMma) || sh.abort) {
             sh.abort = 1;
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t sf_t = tmem_base + static_cast<uint32_t>(SF_COL0 + stage * SF_COLS);
-          const uint32_t fa = smem_u32(sFA + stage * SFA_BYTES);
-          const uint32_t fb = smem_u32(sFB + stage * SFB_BYTES);
-          for (int kk = 0; kk < nat; ++kk) {
-            tmem_cp_32x128b_warpx4(sf_t + kk * 4, smem_desc_sf(fa + kk * ATOM));
-            tmem_cp_32x128b_warpx4(sf_t + 16 + kk * 8, smem_desc_sf(fb + kk * ATOM));
-            tmem_cp_32x128b_warpx4(sf_t + 16 + kk * 8 + 4, smem_desc_sf(fb + (4 + kk) * ATOM));
-          }
           const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
           const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
           for (int kk = 0; kk < nat; ++kk) {
@@ -209,10 +214,53 @@ gemm_nvf4_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
       }
     }
     __syncwarp();
+  } else if (warp < EPI_WARP0) {
+    // scale loaders: lane quarter q = warp % 4. The stage's scale atoms arrive in shared
+    // memory with its TMA tiles (full barrier); the stage's scale columns are free then too,
+    // since the producer refilled the stage only after its previous MMAs completed.
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int64_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      bool ok = true;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        ok = mbar_wait(&sh.full[stage], phase, kErrWaitTimeoutMma);
+        ok = __all_sync(0xffffffffu, ok) && !sh.abort;
+        if (!ok) {
+          sh.abort = 1;
+          break;
+        }
+        const uint4* fa = reinterpret_cast<const uint4*>(sFA + stage * SFA_BYTES) + lane;
+        const uint4* fb = reinterpret_cast<const uint4*>(sFB + stage * SFB_BYTES) + lane;
+        uint32_t va[16], vb[32];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint4 a = fa[kk * (ATOM / 16)];
+          const uint4 b0 = fb[kk * (ATOM / 16)];
+          const uint4 b1 = fb[(4 + kk) * (ATOM / 16)];
+          va[4 * kk] = a.x; va[4 * kk + 1] = a.y; va[4 * kk + 2] = a.z; va[4 * kk + 3] = a.w;
+          vb[8 * kk] = b0.x; vb[8 * kk + 1] = b0.y; vb[8 * kk + 2] = b0.z; vb[8 * kk + 3] = b0.w;
+          vb[8 * kk + 4] = b1.x; vb[8 * kk + 5] = b1.y; vb[8 * kk + 6] = b1.z; vb[8 * kk + 7] = b1.w;
+        }
+        tc_fence_after();
+        const uint32_t col = tmem_base + lane_base + static_cast<uint32_t>(SF_COL0 + stage * SF_COLS);
+        tmem_st_32x32b_x16(col, va);
+        tmem_st_32x32b_x32(col + 16, vb);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.sf_full[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+    }
   } else {
-    // epilogue warps 2..9
+    // epilogue warps 6..13: lane quarter warp % 4, column half (warp - 6) / 4
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int half = (warp - EPI_WARP0) >> 2;
     const int row = quarter * 32 + lane;
     const __nv_bfloat16* bias = static_cast<const __nv_bfloat16*>(p.bias);
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
@@ -230,53 +278,51 @@ gemm_nvf4_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
       tile_coords(t, tiles_m, tiles_n, tm, tn);
       const int64_t m = static_cast<int64_t>(tm) * BM + row;
       const bool row_ok = m < p.M;
+      const int64_t nbase = static_cast<int64_t>(tn) * BN + half * 128;
+      const bool cols_ok = nbase < p.N;  // N % 128 == 0: a 128-column half is all in or all out
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(half * 128);
-      uint32_t r[4][32];
+      const float alpha = row_ok ? __fmul_rn(__ldg(p.sa + m), sb) : 0.0f;
+      const bool gelu = p.epilogue == kEpiGeluTanh;
+      uint32_t pk[64];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tbase + c * 32, r[c]);
-      tmem_ld_wait();
+      for (int c = 0; c < 8; ++c) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(tbase + c * 16, r);
+        tmem_ld_wait();
+        const int64_t n0 = nbase + c * 16;
+        if (row_ok && cols_ok && p.acc_dbg != nullptr) {
+          float* dst = p.acc_dbg + m * p.N + n0;
+#pragma unroll
+          for (int j = 0; j < 16; j += 4)
+            *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                              __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j += 8) {
+          uint32_t bw[4] = {0u, 0u, 0u, 0u};
+          if (bias != nullptr && cols_ok) {
+            const uint4 bu = __ldg(reinterpret_cast<const uint4*>(bias + n0 + j));
+            bw[0] = bu.x; bw[1] = bu.y; bw[2] = bu.z; bw[3] = bu.w;
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float y0 = __fmaf_rn(__uint_as_float(r[j + 2 * e]), alpha, __uint_as_float(bw[e] << 16));
+            float y1 = __fmaf_rn(__uint_as_float(r[j + 2 * e + 1]), alpha, __uint_as_float(bw[e] & 0xffff0000u));
+            if (gelu) {
+              y0 = gi8::gelu_tanh(gi8::bf16_round(y0));
+              y1 = gi8::gelu_tanh(gi8::bf16_round(y1));
+            }
+            pk[8 * c + j / 2 + e] = gi8::pack_bf16x2(y0, y1);
+          }
+        }
+      }
       tc_fence_before();
       mbar_arrive(&sh.tempty);  // the accumulator is in registers: the next tile may start
       aphase ^= 1;
-      if (row_ok) {
-        const float alpha = __fmul_rn(__ldg(p.sa + m), sb);
+      if (row_ok && cols_ok) {
+        uint4* dst = reinterpret_cast<uint4*>(out + m * p.ldo + nbase);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int64_t n0 = static_cast<int64_t>(tn) * BN + half * 128 + c * 32;
-          if (n0 >= p.N) break;
-          if (p.acc_dbg != nullptr) {
-            float* dst = p.acc_dbg + m * p.N + n0;
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[c][j]), __uint_as_float(r[c][j + 1]),
-                                                                __uint_as_float(r[c][j + 2]), __uint_as_float(r[c][j + 3]));
-          }
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            if (bias != nullptr) {
-              const uint4 bu = __ldg(reinterpret_cast<const uint4*>(bias + n0 + j));
-              const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                bv[2 * e] = __uint_as_float(bw[e] << 16);
-                bv[2 * e + 1] = __uint_as_float(bw[e] & 0xffff0000u);
-              }
-            }
-            float y[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              y[e] = __fmaf_rn(__uint_as_float(r[c][j + e]), alpha, bv[e]);
-              if (p.epilogue == kEpiGeluTanh) y[e] = gi8::gelu_tanh(gi8::bf16_round(y[e]));
-            }
-            uint4 o;
-            o.x = gi8::pack_bf16x2(y[0], y[1]);
-            o.y = gi8::pack_bf16x2(y[2], y[3]);
-            o.z = gi8::pack_bf16x2(y[4], y[5]);
-            o.w = gi8::pack_bf16x2(y[6], y[7]);
-            *reinterpret_cast<uint4*>(out + m * p.ldo + n0 + j) = o;
-          }
-        }
+        for (int i = 0; i < 16; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       }
     }
   }

@@ -180,6 +180,18 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
       : "memory");
 }
 
+// 32 lanes x 32 bit, 16 consecutive columns (see tmem_ld_32x32b_x32).
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -217,7 +229,8 @@ __host__ __device__ constexpr uint32_t idesc_nvf4(int m, int n) {
 
 // D[tmem] (+)= (A . SFA) * (B . SFB)^T over K = 64 FP4 elements (32 bytes per row): every 16
 // consecutive K elements of a row share one UE4M3 scale. sfa / sfb are the TMEM addresses of
-// the scale factors (32-lane x 4-column atoms per 128 rows, see tmem_cp_32x128b_warpx4).
+// the scale factors (one 128-row atom = 32 lanes x 4 columns in every lane quarter, lane i
+// holding rows i, i+32, i+64, i+96; see gemm_nvf4.cu).
 __device__ __forceinline__ void mma_nvf4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
   asm volatile(
@@ -229,23 +242,29 @@ __device__ __forceinline__ void mma_nvf4(uint32_t tmem_d, uint64_t adesc, uint64
       : "memory");
 }
 
-// Shared memory -> TMEM copy of one 512-byte scale atom: 32 rows of 16 bytes (the 128x4 tile
-// of the cuBLAS block-scale layout, row r%32 holding rows r, r+32, r+64, r+96), written to 32
-// lanes x 4 columns and replicated into all four lane quarters. Issued by one thread;
-// ordered before the same thread's later tcgen05.mma.
-__device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+// Register -> TMEM stores: thread i of the warp writes lane (quarter*32 + i) of `taddr`'s lane
+// quarter, N consecutive 32-bit columns from taddr's column. Warp-collective.
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
 }
-
-// Shared-memory descriptor of an unswizzled 32 x 16-byte scale atom: 8-row core matrices of
-// 128 contiguous bytes, 128 bytes apart.
-__device__ __forceinline__ uint64_t smem_desc_sf(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr & 0x3FFFF) >> 4);       // start address
-  d |= static_cast<uint64_t>(128 >> 4) << 16;                // LBO (one 16-byte column: unused)
-  d |= static_cast<uint64_t>(128 >> 4) << 32;                // SBO: 8 rows * 16 B
-  d |= static_cast<uint64_t>(1) << 46;                       // descriptor version (sm_100)
-  return d;                                                  // layout: no swizzle (0)
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+      "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+      "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- CTA pairs (cluster of 2)
