@@ -408,20 +408,26 @@ def run_profile_case(args) -> int:
     xsf = torch.empty(((m + 127) // 128 * 128, FFN_H // 16), dtype=torch.uint8, device=dev)
     xs = torch.empty((m,), dtype=torch.float32, device=dev)
     h = torch.empty((m, FFN_F), dtype=torch.bfloat16, device=dev)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for i in range(max(3, args.warmup) + args.steps):
-        if i == max(3, args.warmup):
-            a.record()
+    warm = max(3, args.warmup)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(warm + args.steps)]
+    for i in range(warm + args.steps):
+        ev[i][0].record()
         _native.check(lib.slim_quant_nvfp4_act(x.data_ptr(), _native.BF16, m, FFN_H, 1, xq.data_ptr(), xsf.data_ptr(),
                                                xs.data_ptr(), sp))
+        ev[i][1].record()
         _native.check(lib.slim_gemm_nvfp4(xq.data_ptr(), xsf.data_ptr(), xs.data_ptr(), pw.data_ptr(), pws.data_ptr(),
                                           pwg.data_ptr(), None, h.data_ptr(), None, m, FFN_F, FFN_H,
                                           _native.EPI_SCALE_BIAS, sp))
-    b.record()
+        ev[i][2].record()
     torch.cuda.synchronize(dev)
     assert _native.device_error() == 0
+    timed = ev[warm:]
+    qms = statistics.mean(e[0].elapsed_time(e[1]) for e in timed) if timed else 0.0
+    gms = statistics.mean(e[1].elapsed_time(e[2]) for e in timed) if timed else 0.0
     print(json.dumps({"profile_case": "nvfp4_up_proj", "tokens": m, "steps": args.steps,
-                      "ms_per_step": round(a.elapsed_time(b) / max(1, args.steps), 4)}))
+                      "quant_ms": round(qms, 4), "gemm_ms": round(gms, 4),
+                      "quant_gbs": round((m * FFN_H * 2 + m * FFN_H * 0.5625) / (qms * 1e-3) / 1e9, 1) if qms else None,
+                      "gemm_tops": round(2.0 * m * FFN_H * FFN_F / (gms * 1e-3) / 1e12, 1) if gms else None}))
     return 0
 
 

@@ -48,12 +48,48 @@ def test_weight_pack_bit_exact_vs_oracle(cuda, rows, k, dtype):
     assert bits(ts.cpu().numpy())[0] == bits(np.array([gso], np.float32))[0]
 
 
+def test_pack_codes_at_rounding_ties(cuda):
+    """Elements placed exactly on every E2M1 rounding boundary of their block (x = theta *
+    total, theta in {0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5}) and 1-2 ulps either side: the codes
+    must still equal the oracle's (IEEE quotient, half-to-even), whatever shortcut the kernel
+    takes for the division."""
+    from slimdit import ops
+    rng = np.random.default_rng(77)
+    w = synthetic.weight(256, 512, seed=77)
+    n, k = w.shape
+    w[:, ::16] = np.float32(0.05) * np.sign(rng.standard_normal((n, k // 16))).astype(np.float32)  # block maxima
+    gs = onv.global_scale(np.abs(w).max())
+    blocks = w.reshape(n, k // 16, 16)
+    bamax = np.abs(blocks).max(axis=2)
+    sf = onv.e4m3_encode(np.minimum(((bamax / np.float32(6)).astype(np.float32) / gs).astype(np.float32),
+                                    np.float32(448)))
+    total = (gs * onv.e4m3_decode(sf)).astype(np.float32)
+    thetas = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], np.float32)
+    for j in range(1, 16):
+        th = thetas[rng.integers(0, len(thetas), size=(n, k // 16))]
+        x = (th * total).astype(np.float32)
+        step = rng.integers(-2, 3, size=x.shape)
+        for _ in range(2):
+            x = np.where(step > 0, np.nextafter(x, np.float32(np.inf)), x)
+            x = np.where(step < 0, np.nextafter(x, np.float32(0)), x)
+            step = step - np.sign(step)
+        sign = np.where(rng.random(x.shape) < 0.5, np.float32(-1), np.float32(1))
+        blocks[:, :, j] = np.where(np.abs(x) < bamax, sign * x, blocks[:, :, j])
+    w = blocks.reshape(n, k)
+    q, sfd, ts = ops.nvfp4_pack(to_dev(w, cuda))
+    qo, sfo, gso = onv.quantize_nvfp4_weight(w)
+    assert np.array_equal(sfd.cpu().numpy(), sfo) and ts.cpu().numpy()[0] == gso
+    got, want = onv.unpack_nibbles(q.cpu().numpy()), onv.unpack_nibbles(qo)
+    assert np.array_equal(got, want), f"{int((got != want).sum())} codes differ at rounding ties"
+
+
 @pytest.mark.parametrize("m,k,rotate,dtype", [
     (1, 64, False, torch.bfloat16),        # one row, one scale tile column
     (77, 5120, True, torch.bfloat16),      # ragged rows, config K, rotated
     (300, 1024, False, torch.float32),
     (128, 13824, True, torch.bfloat16),    # FFN hidden width
     (200, 256, True, torch.float16),
+    (40, 16384, True, torch.float32),      # widest row: fewer rows staged in shared memory
 ])
 def test_activation_quant_bit_exact_vs_oracle(cuda, m, k, rotate, dtype):
     from slimdit import ops

@@ -20,6 +20,7 @@
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <cstdint>
 
 #include "slim_kernels.h"
@@ -52,7 +53,25 @@ __device__ __forceinline__ uint32_t e2m1_code(float v) {
   return c | ((__float_as_uint(v) >> 28) & 8u);
 }
 
+// E2M1 magnitude code of a >= 0 by region scaling: the grid has step 1/2 below 2, 1 in
+// [2, 4) and 2 above, so code = base + rint(a * scale) with (scale, base) = (2, 0), (1, 2),
+// (1/2, 4), saturating at 7. rint (round half to even on a*scale, exact since the scales are
+// powers of two) gives exactly the grid's half-to-even ties: 0.25 -> 0, 0.75 -> 1.0,
+// 1.25 -> 1.0, 1.75 -> 2.0, 2.5 -> 2.0, 3.5 -> 4.0, 5 -> 4.0. `frac` returns |a*scale - rint|.
+__device__ __forceinline__ uint32_t e2m1_mag(float a, float& frac) {
+  const float scale = a < 2.0f ? 2.0f : (a < 4.0f ? 1.0f : 0.5f);
+  const uint32_t base = a < 2.0f ? 0u : (a < 4.0f ? 2u : 4u);
+  const float s = __fmul_rn(a, scale);
+  const float r = rintf(s);
+  frac = fabsf(__fsub_rn(s, r));
+  return min(base + static_cast<uint32_t>(r), 7u);
+}
+
 // One 16-element block -> 8 packed bytes and its scale byte.
+// The element quotient v = fl(x / total) is not formed: t = |x| * fl(1/total) is within
+// 2^-22 |v| of |v| (two roundings), so e2m1_mag(t) equals e2m1_mag(|v|) unless t*scale lies
+// within 2^-18 of a half-integer (a rounding boundary); those elements (about 1e-5 of them)
+// take the IEEE division. The sign is x's (a zero quotient keeps x's sign, as the division's).
 __device__ __forceinline__ void quant_block16(const float (&v)[16], float gs, uint2& packed, uint32_t& sfb) {
   float bm = 0.0f;
 #pragma unroll
@@ -65,25 +84,55 @@ __device__ __forceinline__ void quant_block16(const float (&v)[16], float gs, ui
   const float total = __fmul_rn(gs, e4m3_value(sfb));
   uint32_t w[2] = {0u, 0u};
   if (total != 0.0f) {
+    const float rcp = __frcp_rn(total);
+    uint32_t slow = 0;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) w[i >> 3] |= e2m1_code(__fdiv_rn(v[i], total)) << (4 * (i & 7));
+    for (int i = 0; i < 16; ++i) {
+      float frac;
+      const uint32_t mag = e2m1_mag(__fmul_rn(fabsf(v[i]), rcp), frac);
+      slow |= static_cast<uint32_t>(frac > 0.5f - 7.62939453125e-6f) << i;  // 2^-17 margin
+      w[i >> 3] |= (mag | ((__float_as_uint(v[i]) >> 28) & 8u)) << (4 * (i & 7));
+    }
+    if (slow != 0u) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if ((slow >> i) & 1u) {
+          const uint32_t code = e2m1_code(__fdiv_rn(v[i], total));
+          const uint32_t sh = 4 * (i & 7);
+          w[i >> 3] = (w[i >> 3] & ~(15u << sh)) | (code << sh);
+        }
+      }
+    }
   }
   packed = make_uint2(w[0], w[1]);
 }
 
+// A thread's 16 input elements as raw 16-byte words (4 for fp32, 2 for 16-bit types): loaded
+// one row ahead so the next row's HBM reads overlap this row's arithmetic.
 template <int DT>
-__device__ __forceinline__ void load16(const void* x, int64_t e0, float (&f)[16]) {
+struct Raw16 {
+  uint4 w[DT == kF32 ? 4 : 2];
+};
+
+template <int DT>
+__device__ __forceinline__ Raw16<DT> load_raw16(const void* x, int64_t e0) {
+  Raw16<DT> r;
+  const uint4* p = reinterpret_cast<const uint4*>(static_cast<const unsigned char*>(x) + e0 * (DT == kF32 ? 4 : 2));
+#pragma unroll
+  for (int e = 0; e < (DT == kF32 ? 4 : 2); ++e) r.w[e] = __ldg(p + e);
+  return r;
+}
+
+template <int DT>
+__device__ __forceinline__ void unpack16(const Raw16<DT>& r, float (&f)[16]) {
   if (DT == kF32) {
-    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + e0);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float4 g = __ldg(p + e);
-      f[4 * e] = g.x; f[4 * e + 1] = g.y; f[4 * e + 2] = g.z; f[4 * e + 3] = g.w;
+      f[4 * e] = __uint_as_float(r.w[e].x); f[4 * e + 1] = __uint_as_float(r.w[e].y);
+      f[4 * e + 2] = __uint_as_float(r.w[e].z); f[4 * e + 3] = __uint_as_float(r.w[e].w);
     }
   } else {
-    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const unsigned short*>(x) + e0);
-    const uint4 u0 = __ldg(p), u1 = __ldg(p + 1);
-    const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    const uint32_t w[8] = {r.w[0].x, r.w[0].y, r.w[0].z, r.w[0].w, r.w[1].x, r.w[1].y, r.w[1].z, r.w[1].w};
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       if (DT == kBF16) {
@@ -95,6 +144,11 @@ __device__ __forceinline__ void load16(const void* x, int64_t e0, float (&f)[16]
       }
     }
   }
+}
+
+template <int DT>
+__device__ __forceinline__ void load16(const void* x, int64_t e0, float (&f)[16]) {
+  unpack16<DT>(load_raw16<DT>(x, e0), f);
 }
 
 // Radix-4 butterfly step b_i = ((a0 + a1) + (a2 + a3)) - 2*a_{3-i}, each operation rounded
@@ -122,16 +176,37 @@ __device__ __forceinline__ int xpos(int row, int col) {
 }
 
 // One CTA per row (persistent over rows), thread c owns 16-element block c of the row.
-// Rows in [rows, rows_pad) only get zero scale bytes (padding of the last 128-row tile).
+// Rows are staged in shared memory by bulk copies, nst (1..3, as many as shared memory holds)
+// rows ahead: the HBM reads of the next rows overlap this row's arithmetic without holding
+// registers. Rows in [rows, rows_pad)
+// only get zero scale bytes (padding of the last 128-row tile).
 // ROW_SCALE: global scale per row (written to row_scale); else per tensor from *amax_in.
+constexpr int kQuantMaxStages = 3;
+
+template <int DT>
+__device__ __forceinline__ Raw16<DT> smem_raw16(const unsigned char* stage, int t) {
+  Raw16<DT> r;
+  const uint4* p = reinterpret_cast<const uint4*>(stage) + t * (DT == kF32 ? 4 : 2);
+#pragma unroll
+  for (int e = 0; e < (DT == kF32 ? 4 : 2); ++e) r.w[e] = p[e];
+  return r;
+}
+
 template <int DT, bool ROT, bool ROW_SCALE>
 __global__ void __launch_bounds__(1024) nvfp4_quant_kernel(const void* __restrict__ x, int64_t rows,
                                                            int64_t rows_pad, int K,
                                                            const float* __restrict__ amax_in,
                                                            uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
-                                                           float* __restrict__ row_scale) {
-  extern __shared__ __align__(16) float xch[];
+                                                           float* __restrict__ row_scale, int nst) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ float red[2][32];
+  const int NST = nst;
+  constexpr int kEsz = DT == kF32 ? 4 : 2;
+  const uint32_t row_bytes = static_cast<uint32_t>(K) * kEsz;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);                   // up to 3 mbarriers
+  unsigned char* stages = smem_raw + 32;                                   // NST staged rows
+  float* xch = reinterpret_cast<float*>(stages + NST * static_cast<size_t>(row_bytes));
+  const unsigned char* src = static_cast<const unsigned char*>(x);
   const int t = threadIdx.x;
   const int nb = K >> 4;
   const int ctiles = K >> 6;
@@ -142,15 +217,37 @@ __global__ void __launch_bounds__(1024) nvfp4_quant_kernel(const void* __restric
   if (!ROW_SCALE) gs_tensor = __fdiv_rn(__ldg(amax_in), 2688.0f);
   float* g = xch + (t >> 4) * 272;
   const int r = t & 15;
+
+  if (t == 0) {
+    for (int b = 0; b < NST; ++b) mbar_init(&bar[b], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  uint32_t pending = 0, pending_parity = 0;
+  if (t == 0) {
+    for (int b = 0; b < NST; ++b) {
+      const int64_t rb = blockIdx.x + static_cast<int64_t>(b) * gridDim.x;
+      if (rb < rows) {
+        mbar_arrive_expect_tx(&bar[b], row_bytes);
+        bulk_load(stages + b * static_cast<size_t>(row_bytes), src + rb * row_bytes, row_bytes, &bar[b]);
+        pending |= 1u << b;
+      }
+    }
+  }
   int it = 0;
   for (int64_t row = blockIdx.x; row < rows_pad; row += gridDim.x, ++it) {
     if (row >= rows) {
       if (act) sf[blocked_offset(row, t, ctiles)] = 0;
       continue;
     }
+    const int b = it % NST;
+    const bool ok = mbar_wait(&bar[b], static_cast<uint32_t>(it / NST) & 1u, kErrWaitTimeoutProducer);
+    if (ok && t == 0) pending &= ~(1u << b);
+    if (__syncthreads_or(!ok)) break;  // a staged row never arrived: stop (error recorded)
+    const unsigned char* stage = stages + b * static_cast<size_t>(row_bytes);
     float v[16];
     if (act) {
-      load16<DT>(x, row * K + 16 * t, v);
+      unpack16<DT>(smem_raw16<DT>(stage, t), v);
     } else {
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] = 0.0f;
@@ -194,6 +291,18 @@ __global__ void __launch_bounds__(1024) nvfp4_quant_kernel(const void* __restric
       const float rm = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < nw ? __float_as_uint(red[it & 1][lane]) : 0u));
       gs = __fdiv_rn(rm, 2688.0f);
       if (t == 0) row_scale[row] = gs;
+    } else {
+      __syncthreads();
+    }
+    // every thread has read this row's stage: refill it with the row NST iterations ahead
+    if (t == 0) {
+      const int64_t rn = row + static_cast<int64_t>(NST) * gridDim.x;
+      if (rn < rows) {
+        mbar_arrive_expect_tx(&bar[b], row_bytes);
+        bulk_load(stages + b * static_cast<size_t>(row_bytes), src + rn * row_bytes, row_bytes, &bar[b]);
+        pending |= 1u << b;
+        pending_parity = (pending_parity & ~(1u << b)) | (((static_cast<uint32_t>(it / NST) + 1u) & 1u) << b);
+      }
     }
     if (act) {
       uint2 packed;
@@ -202,6 +311,10 @@ __global__ void __launch_bounds__(1024) nvfp4_quant_kernel(const void* __restric
       *reinterpret_cast<uint2*>(q + row * (K >> 1) + 8 * t) = packed;
       sf[blocked_offset(row, t, ctiles)] = static_cast<uint8_t>(sfb);
     }
+  }
+  if (t == 0) {
+    for (int b = 0; b < NST; ++b)
+      if (pending & (1u << b)) mbar_wait(&bar[b], (pending_parity >> b) & 1u, kErrWaitTimeoutDrain);
   }
 }
 
@@ -314,7 +427,12 @@ template <int DT, bool ROT, bool ROW_SCALE>
 static cudaError_t launch_quant_t(const void* x, int64_t rows, int64_t rows_pad, int K, const float* amax_in,
                                   uint8_t* q, uint8_t* sf, float* row_scale, cudaStream_t st) {
   const int threads = ((K >> 4) + 31) / 32 * 32;
-  const size_t smem = ROT ? static_cast<size_t>(threads / 16) * 272 * sizeof(float) : 0;
+  const size_t row_bytes = static_cast<size_t>(K) * (DT == kF32 ? 4 : 2);
+  const size_t fixed = 32 + (ROT ? static_cast<size_t>(threads / 16) * 272 * sizeof(float) : 0);
+  constexpr size_t kMaxSmem = 232448 - 256;  // opt-in maximum minus the static reduction buffer
+  const int nst = static_cast<int>(std::min<size_t>(kQuantMaxStages, (kMaxSmem - fixed) / row_bytes));
+  if (nst < 1) return cudaErrorInvalidValue;
+  const size_t smem = fixed + static_cast<size_t>(nst) * row_bytes;
   auto fn = nvfp4_quant_kernel<DT, ROT, ROW_SCALE>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -326,7 +444,7 @@ static cudaError_t launch_quant_t(const void* x, int64_t rows, int64_t rows_pad,
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm;
   const int grid = static_cast<int>(rows_pad < cap ? rows_pad : cap);
-  fn<<<grid, threads, smem, st>>>(x, rows, rows_pad, K, amax_in, q, sf, row_scale);
+  fn<<<grid, threads, smem, st>>>(x, rows, rows_pad, K, amax_in, q, sf, row_scale, nst);
   return cudaGetLastError();
 }
 
