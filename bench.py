@@ -382,6 +382,53 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
         "algorithmic_bytes": int(fp4_bytes), "bytes_moved_two_pass": int(fp4_bytes + 2 * elems), "scaling": "strong"}
     del ws, pq, psf, pts
     torch.cuda.empty_cache()
+
+    # ---- output-column split (N > 1 only): config-1 linear, weight rows split over the ranks,
+    # x replicated, column blocks all-gathered over NVLink (NCCL), "blocks" layout
+    if world > 1:
+        import torch.distributed as dist
+
+        from slimdit import colsplit
+
+        xs, qw, sw, bias = make_inputs(torch, dev, seed=200)
+        q_s, s_s, b_s = colsplit.shard_weight(qw, sw, bias, rank, world)
+        del qw, sw, bias
+        nl = N // world
+        y_loc = torch.empty((M, nl), dtype=torch.bfloat16, device=dev)
+        blocks = torch.empty((world * M, nl), dtype=torch.bfloat16, device=dev)
+        xq = torch.empty((M, K), dtype=torch.int8, device=dev)
+        sx = torch.empty((M,), dtype=torch.float32, device=dev)
+
+        def cs_step(ev_mid=None):
+            _native.check(lib.slim_int8_linear(xs.data_ptr(), _native.BF16, q_s.data_ptr(), s_s.data_ptr(),
+                                               b_s.data_ptr(), y_loc.data_ptr(), xq.data_ptr(), sx.data_ptr(), M, nl,
+                                               K, 256, _native.EPI_SCALE_BIAS, sp))
+            if ev_mid is not None:
+                ev_mid.record(stream)
+            dist.all_gather_into_tensor(blocks, y_loc)
+
+        for _ in range(3):
+            cs_step()
+        torch.cuda.synchronize(dev)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        mids = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        e0.record(stream)
+        for i in range(steps):
+            cs_step(mids[i])
+            ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+        ms = reduce_max(e0.elapsed_time(ends[-1]) / steps)
+        gather_ms = reduce_max(sum(mids[i].elapsed_time(ends[i]) for i in range(steps)) / steps)
+        out["colsplit_linear"] = {
+            "workload": f"config-1 linear, W rows split {world} ways, x replicated, NCCL all-gather of "
+                        f"[{M},{nl}] bf16 blocks",
+            "ms_per_step": round(ms, 4), "allgather_ms": round(gather_ms, 4),
+            "value": round(OPS_PER_STEP / (ms * 1e-3) / 1e12, 1), "unit": "TOPS", "scaling": "strong",
+            "allgather_busbw_gbs": round((world - 1) * M * nl * 2 / (gather_ms * 1e-3) / 1e9, 1), "steps": steps}
+        del xs, q_s, s_s, b_s, y_loc, blocks, xq, sx
+        torch.cuda.empty_cache()
     return out
 
 
