@@ -553,12 +553,10 @@ def run_ours(args) -> int:
 
         x_h = x.cpu().pin_memory()
         out_h = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
-        x_d = torch.empty_like(x)
+        x_d = None
 
         def e2e_step():
-            x_d.copy_(x_h, non_blocking=True)
-            y = ops.int8_linear(x_d, qw, sw, bias=bias)
-            out_h.copy_(y, non_blocking=True)
+            ops.int8_linear_host(x_h, qw, sw, bias=bias, out=out_h)
 
         for _ in range(2):
             e2e_step()
@@ -649,7 +647,9 @@ def run_ours(args) -> int:
         if e2e is not None:
             line["e2e"] = {"value": round(world * OPS_PER_STEP / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TOPS",
                            "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                           "ms_per_step": round(e2e_ms, 3), "api": "slimdit.ops.int8_linear, pinned host buffers"}
+                           "ms_per_step": round(e2e_ms, 3),
+                           "api": "slimdit.ops.int8_linear_host: pinned host x and out, H2D / linear / D2H of "
+                                  "4096-row chunks overlapped on three streams"}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         print(json.dumps(line), flush=True)

@@ -168,3 +168,23 @@ def test_ffn_pair_vs_oracle(cuda):
     yv = y.float().cpu().numpy()
     rel = np.linalg.norm(yv - ref) / np.linalg.norm(ref)
     assert rel < 1e-2, rel
+
+
+@pytest.mark.parametrize("m,chunk,pinned", [(10000, 4096, True), (300, 128, False), (5, 4096, True)])
+def test_int8_linear_host_pipelined_equals_device_call(cuda, m, chunk, pinned):
+    """Host-memory activations through the chunked, stream-overlapped path: the same bytes as
+    the single device call (token rows are independent)."""
+    from slimdit import ops
+    from slimdit.int8 import quantize_convrot_weight
+    x = synthetic.activations(m, 1024, seed=m)
+    w = synthetic.weight(768, 1024, seed=9)
+    qw, sw = quantize_convrot_weight(w)
+    qw_d, sw_d = torch.from_numpy(qw).to(cuda), torch.from_numpy(sw).to(cuda)
+    bias = torch.from_numpy(np.random.default_rng(4).standard_normal(768).astype(np.float32) * 0.02).to(torch.bfloat16)
+    xh = torch.from_numpy(x).to(torch.bfloat16)
+    if pinned:
+        xh = xh.pin_memory()
+    y = ops.int8_linear_host(xh, qw_d, sw_d, bias=bias, chunk_rows=chunk)
+    torch.cuda.current_stream(cuda).synchronize()
+    ref = ops.int8_linear(xh.to(cuda), qw_d, sw_d, bias=bias.to(cuda)).cpu()
+    assert y.device.type == "cpu" and torch.equal(y, ref)

@@ -11,6 +11,10 @@ computation runs in libslimdit_b200.so).
 * ``int8_linear``   the convrot W8A8 linear, same call shape as the runtime op the reference
                     benchmarks (``comfy_kitchen.int8_linear``, tools/bench_int8.py:65-68)
 * ``ffn_int8``      up-proj -> GELU-tanh -> rotate + requant -> down-proj
+* ``int8_linear_host``  the linear on host-resident activations, copies and compute of row
+                    chunks overlapped on three streams
+* ``nvfp4_pack`` / ``nvfp4_quantize_act`` / ``nvfp4_dequantize`` / ``nvfp4_error`` /
+  ``gemm_nvfp4`` / ``nvfp4_linear``  the NVFP4 format of slimdit/nvfp4.py and its linear
 """
 
 from __future__ import annotations
@@ -189,6 +193,96 @@ def ffn_int8(x: torch.Tensor, w_up: torch.Tensor, s_up: torch.Tensor, w_down: to
     """
     h = int8_linear(x, w_up, s_up, bias=b_up, epilogue="gelu_tanh")
     return int8_linear(h, w_down, s_down, bias=b_down)
+
+
+_PIPE_STREAMS: dict[int, tuple] = {}
+
+
+def _pipe_streams(dev: torch.device):
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    if idx not in _PIPE_STREAMS:
+        _PIPE_STREAMS[idx] = tuple(torch.cuda.Stream(device=idx) for _ in range(3))
+    return _PIPE_STREAMS[idx]
+
+
+def int8_linear_host(x: torch.Tensor, qweight: torch.Tensor, wscales: torch.Tensor, bias: torch.Tensor | None = None,
+                     out: torch.Tensor | None = None, chunk_rows: int = 4096, convrot_groupsize: int = 256,
+                     epilogue: str | None = None) -> torch.Tensor:
+    """The convrot linear for activations in host memory: y_host = int8_linear(x_host) on the
+    weight's GPU, with the host->device copy, the linear and the device->host copy of
+    successive row chunks overlapped on three streams (two device buffers per direction).
+
+    x: host [M, K] bf16/f16/f32 (pinned for asynchronous copies); out: host bf16 [M, N]
+    (allocated pinned when x is pinned, if not given). Token rows are independent, so the
+    result equals int8_linear on the whole batch bit for bit. The copies into `out` are
+    asynchronous with respect to the host, like non_blocking copies: synchronise the current
+    stream before reading it.
+    """
+    nat.require_cuda()
+    if x.is_cuda or x.dim() != 2:
+        raise TypeError("x must be a 2-D host tensor")
+    if x.dtype not in _DT:
+        raise TypeError(f"unsupported activation dtype {x.dtype}")
+    qweight = _cuda2d(qweight, "qweight")
+    dev = qweight.device
+    m, k = x.shape
+    n = qweight.shape[0]
+    if qweight.shape[1] != k:
+        raise ValueError(f"in_features mismatch: x [..., {k}] vs qweight {tuple(qweight.shape)}")
+    if epilogue not in _EPI:
+        raise ValueError(f"epilogue must be one of {sorted(str(e) for e in _EPI)}")
+    if chunk_rows <= 0:
+        raise ValueError("chunk_rows must be positive")
+    sw = _vec(wscales, n, torch.float32, dev, "wscales")
+    b = _vec(bias, n, torch.bfloat16, dev, "bias")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, pin_memory=x.is_pinned())
+    elif out.is_cuda or out.shape != (m, n) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous host bf16 [M, N] tensor")
+    if m == 0:
+        return out
+    x = x.contiguous()
+    chunk = min(chunk_rows, m)
+    s_h2d, s_cmp, s_d2h = _pipe_streams(dev)
+    cur = torch.cuda.current_stream(dev)
+    lib = nat.load()
+    with torch.cuda.device(dev):
+        xb = [torch.empty((chunk, k), dtype=x.dtype, device=dev) for _ in range(2)]
+        yb = [torch.empty((chunk, n), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        xq = torch.empty((chunk, k), dtype=torch.int8, device=dev)
+        sx = torch.empty((chunk,), dtype=torch.float32, device=dev)
+        ev_h2d = [torch.cuda.Event() for _ in range(2)]
+        ev_cmp = [torch.cuda.Event() for _ in range(2)]
+        ev_d2h = [torch.cuda.Event() for _ in range(2)]
+        for s in (s_h2d, s_cmp, s_d2h):
+            s.wait_stream(cur)  # weights, scales and buffers come from the current stream
+        for i, r0 in enumerate(range(0, m, chunk)):
+            j = i % 2
+            rows = min(chunk, m - r0)
+            with torch.cuda.stream(s_h2d):
+                if i >= 2:
+                    s_h2d.wait_event(ev_cmp[j])      # the linear of chunk i-2 has read xb[j]
+                xb[j][:rows].copy_(x[r0:r0 + rows], non_blocking=True)
+                ev_h2d[j].record(s_h2d)
+            s_cmp.wait_event(ev_h2d[j])
+            if i >= 2:
+                s_cmp.wait_event(ev_d2h[j])          # chunk i-2's output has left yb[j]
+            nat.check(lib.slim_int8_linear(xb[j].data_ptr(), _DT[x.dtype], qweight.data_ptr(), sw.data_ptr(), _ptr(b),
+                                           yb[j].data_ptr(), xq.data_ptr(), sx.data_ptr(), rows, n, k,
+                                           convrot_groupsize, _EPI[epilogue], s_cmp.cuda_stream))
+            ev_cmp[j].record(s_cmp)
+            with torch.cuda.stream(s_d2h):
+                s_d2h.wait_event(ev_cmp[j])
+                out[r0:r0 + rows].copy_(yb[j][:rows], non_blocking=True)
+                ev_d2h[j].record(s_d2h)
+        for t in (*xb, *yb, xq, sx, sw, qweight, *( [b] if b is not None else [])):
+            t.record_stream(s_h2d)
+            t.record_stream(s_cmp)
+            t.record_stream(s_d2h)
+        cur.wait_stream(s_d2h)
+        cur.wait_stream(s_cmp)
+        cur.wait_stream(s_h2d)
+    return out
 
 
 # ---------------------------------------------------------------- NVFP4
