@@ -427,7 +427,31 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
             "ms_per_step": round(ms, 4), "allgather_ms": round(gather_ms, 4),
             "value": round(OPS_PER_STEP / (ms * 1e-3) / 1e12, 1), "unit": "TOPS", "scaling": "strong",
             "allgather_busbw_gbs": round((world - 1) * M * nl * 2 / (gather_ms * 1e-3) / 1e9, 1), "steps": steps}
-        del xs, q_s, s_s, b_s, y_loc, blocks, xq, sx
+        del y_loc, blocks, xq, sx
+        torch.cuda.empty_cache()
+        # the same split with the all-gather inside the GEMM epilogue (peer stores over NVLink)
+        for mode, what in (("dma", "4096-row chunks, each pushed to every peer by the copy engines while the next "
+                                   "chunk computes"),
+                           ("stores", "the GEMM epilogue stores each tile into every peer's output")):
+            fused = colsplit.PeerColumnSplit(M, N, K, device=dev, mode=mode)
+            for _ in range(3):
+                fused(xs, q_s, s_s, b_s)
+            torch.cuda.synchronize(dev)
+            barrier()
+            e0.record(stream)
+            for i in range(steps):
+                fused(xs, q_s, s_s, b_s)
+            ends[0].record(stream)
+            torch.cuda.synchronize(dev)
+            ms = reduce_max(e0.elapsed_time(ends[0]) / steps)
+            out[f"colsplit_linear_peer_{mode}"] = {
+                "workload": f"config-1 linear, W rows split {world} ways, x replicated, written into all {world} "
+                            f"GPUs' [{M},{N}] outputs over NVLink (CUDA IPC mappings): {what}",
+                "ms_per_step": round(ms, 4), "value": round(OPS_PER_STEP / (ms * 1e-3) / 1e12, 1), "unit": "TOPS",
+                "scaling": "strong", "nvlink_bytes_out_per_gpu": (world - 1) * M * nl * 2, "steps": steps}
+            fused.close()
+            del fused
+        del xs, q_s, s_s, b_s
         torch.cuda.empty_cache()
     return out
 

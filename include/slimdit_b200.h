@@ -121,6 +121,41 @@ int slim_int8_linear_noalloc(const void* x, int x_dtype, const int8_t* qw, const
                              const void* bias, void* out, int64_t M, int64_t N, int64_t K,
                              int group, int epilogue, void* stream);
 
+/* Allocates `bytes` of device memory on the current device that other processes can map
+ * (cudaMalloc + cudaIpcGetMemHandle): *ptr receives the buffer, ipc_handle (64 bytes) its
+ * CUDA IPC handle for slim_peer_open in the other processes. Free with
+ * slim_peer_buffer_free after every process has closed its mapping. */
+int slim_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+int slim_peer_buffer_free(void* ptr);
+
+/* Maps another process's device allocation into this process on the current device (CUDA
+ * IPC, peer access over NVLink enabled on first use): ipc_handle is the 64-byte
+ * cudaIpcMemHandle_t of the allocation, offset the byte offset of the buffer inside it.
+ * *ptr receives the mapped buffer address. Plain peer mapping: no multicast object. */
+int slim_peer_open(const void* ipc_handle, int64_t offset, void** ptr);
+
+/* Unmaps a buffer opened by slim_peer_open (ptr and offset as returned and given there). */
+int slim_peer_close(void* ptr, int64_t offset);
+
+/* Stream-ordered 2-D copy of `height` rows of `width` bytes between any two device buffers
+ * of this process (local or peer-mapped; the copy engines move it over NVLink). */
+int slim_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width,
+                 int64_t height, void* stream);
+
+/* The convrot linear with its output columns split over the GPUs of a node: this GPU
+ * computes y[:, c0:c0+N] for its weight rows qw/sw/bias [N, K] (x [M, K] replicated) and the
+ * GEMM epilogue stores every output tile into each of the n_outs buffers `outs` (host array of
+ * device pointers: this GPU's output and the other GPUs' outputs mapped into this process,
+ * e.g. symmetric memory over NVLink), each already offset to column c0, rows ldo elements
+ * apart. The all-gather of the reference plan (an NCCL collective after the GEMM) happens
+ * inside the GEMM, tile by tile. The caller synchronises the GPUs after the call (all ranks'
+ * stores done) before reading. n_outs <= 8. No reference counterpart: the reference runs
+ * one GPU; this is the optional output-column split of the B200 plan. */
+int slim_int8_linear_colsplit(const void* x, int x_dtype, const int8_t* qw, const float* sw,
+                              const void* bias, void* const* outs, int n_outs, int64_t ldo,
+                              int8_t* xq_ws, float* sx_ws, int64_t M, int64_t N, int64_t K,
+                              int group, int epilogue, void* stream);
+
 /* ---------------------------------------------------------------- NVFP4
  * Format of slimdit/nvfp4.py:3-8: E2M1 codes packed two per byte (element 2i in the low
  * nibble), one UE4M3 scale per 16 consecutive elements along K stored in the cuBLAS 128x4

@@ -1,8 +1,9 @@
 """Multi-GPU paths on 2 GPUs of one node (skipped when fewer are visible).
 
 * output-column split (slimdit/colsplit.py): each rank computes its column block with the
-  CUDA linear and NCCL all-gathers them; the result must equal, bit for bit, the
-  single-GPU linear on the full weight computed on the same rank.
+  CUDA linear and NCCL all-gathers them, or (PeerColumnSplit) its GEMM epilogue stores the
+  tiles into every rank's output over NVLink; either way the result must equal, bit for bit,
+  the single-GPU linear on the full weight computed on the same rank.
 """
 
 import os
@@ -49,6 +50,19 @@ def _worker(rank, world, port, result_dir):
         assert torch.equal(rows, full)
         for g in range(world):
             assert torch.equal(blocks[g], full[:, g * n // world:(g + 1) * n // world])
+        # the all-gather inside the GEMM epilogue (peer stores over NVLink)
+        for mode in ("dma", "stores"):
+            fused = colsplit.PeerColumnSplit(m, n, k, device=dev, mode=mode, chunk_rows=384)
+            try:
+                for _ in range(2):  # twice: the buffer is reused
+                    y = fused(x, q_s, s_s, b_s)
+                    torch.cuda.synchronize(dev)
+                    assert torch.equal(y, full), mode
+                y = fused(x[:37], q_s, s_s, b_s)
+                torch.cuda.synchronize(dev)
+                assert torch.equal(y, full[:37]), mode
+            finally:
+                fused.close()
         assert _native.device_error() == 0
         Path(result_dir, f"ok{rank}").write_text("ok")
     finally:

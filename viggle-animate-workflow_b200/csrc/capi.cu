@@ -235,4 +235,89 @@ int slim_int8_linear(const void* x, int x_dtype, const int8_t* qw, const float* 
   return SLIM_OK;
 }
 
+int slim_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  if (ptr == nullptr || ipc_handle == nullptr) return fail(SLIM_ERR_NULL, "ptr/ipc_handle is NULL");
+  if (bytes == 0) return fail(SLIM_ERR_SHAPE, "empty peer buffer");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc of the peer buffer");
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "cudaIpcGetMemHandle");
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return SLIM_OK;
+}
+
+int slim_peer_buffer_free(void* ptr) {
+  if (ptr == nullptr) return SLIM_OK;
+  cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFree of the peer buffer");
+  return SLIM_OK;
+}
+
+int slim_peer_open(const void* ipc_handle, int64_t offset, void** ptr) {
+  if (ipc_handle == nullptr || ptr == nullptr) return fail(SLIM_ERR_NULL, "ipc_handle/ptr is NULL");
+  if (offset < 0 || offset % 16 != 0) return fail(SLIM_ERR_ALIGN, "offset %lld must be a non-negative multiple of 16", static_cast<long long>(offset));
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *ptr = static_cast<char*>(base) + offset;
+  return SLIM_OK;
+}
+
+int slim_peer_close(void* ptr, int64_t offset) {
+  if (ptr == nullptr) return fail(SLIM_ERR_NULL, "ptr is NULL");
+  cudaError_t e = cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return SLIM_OK;
+}
+
+int slim_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
+                 void* stream) {
+  if (height == 0 || width == 0) return SLIM_OK;
+  if (dst == nullptr || src == nullptr) return fail(SLIM_ERR_NULL, "dst/src is NULL");
+  if (width < 0 || height < 0 || dpitch < width || spitch < width) return fail(SLIM_ERR_SHAPE, "bad 2-D copy geometry");
+  cudaError_t e = cudaMemcpy2DAsync(dst, static_cast<size_t>(dpitch), src, static_cast<size_t>(spitch),
+                                    static_cast<size_t>(width), static_cast<size_t>(height), cudaMemcpyDefault,
+                                    static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy2DAsync");
+  return SLIM_OK;
+}
+
+int slim_int8_linear_colsplit(const void* x, int x_dtype, const int8_t* qw, const float* sw, const void* bias,
+                              void* const* outs, int n_outs, int64_t ldo, int8_t* xq_ws, float* sx_ws, int64_t M,
+                              int64_t N, int64_t K, int group, int epilogue, void* stream) {
+  int rc;
+  if (outs == nullptr || n_outs < 1 || n_outs > kMaxPeers + 1)
+    return fail(SLIM_ERR_SHAPE, "n_outs must be 1..%d, got %d", kMaxPeers + 1, n_outs);
+  for (int i = 0; i < n_outs; ++i)
+    if (outs[i] == nullptr || !aligned16(outs[i])) return fail(SLIM_ERR_ALIGN, "output %d is NULL or not 16-byte aligned", i);
+  if (ldo < N || ldo % 8 != 0) return fail(SLIM_ERR_SHAPE, "ldo=%lld must be >= N and a multiple of 8", static_cast<long long>(ldo));
+  if ((rc = check_group(K, group)) != SLIM_OK) return rc;
+  if ((rc = check_dtype(x_dtype)) != SLIM_OK) return rc;
+  if (K > 16384) return fail(SLIM_ERR_SHAPE, "in_features above 16384 not supported by the activation quantiser");
+  if ((rc = gemm_checks(xq_ws, qw, sx_ws, sw, bias, outs[0], nullptr, M, N, K, epilogue)) != SLIM_OK) return rc;
+  if (M == 0) return SLIM_OK;
+  if (x == nullptr) return fail(SLIM_ERR_NULL, "x is NULL");
+  if (!aligned16(x)) return fail(SLIM_ERR_ALIGN, "x must be 16-byte aligned");
+  if ((rc = check_arch()) != SLIM_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_bfly_rotate_quant(x, x_dtype, M, static_cast<int>(K), xq_ws, sx_ws, nullptr, st);
+  if (e != cudaSuccess) return cuda_fail(e, "activation quant launch");
+  note_launch();
+  GemmI8Params p{xq_ws, qw, sx_ws, sw, bias, outs[0], nullptr, M, N, K, ldo, epilogue};
+  p.n_peer = n_outs - 1;
+  for (int i = 1; i < n_outs; ++i) p.peer_out[i - 1] = outs[i];
+  e = launch_gemm_i8(p, st);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+  note_launch();
+  return SLIM_OK;
+}
+
 }  // extern "C"

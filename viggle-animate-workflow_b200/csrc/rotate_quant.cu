@@ -331,7 +331,7 @@ __device__ __forceinline__ uint32_t quant_pair(float2 S, float2 r16x2, float sca
 // of float2 registers through all four radix-4 stages. Rows are staged into shared memory by
 // double-buffered bulk copies. One block barrier per row (partial maxima double-buffered).
 template <int DT>
-__global__ void __launch_bounds__(512) bfly2_rotate_quant_kernel(const void* __restrict__ x,
+__global__ void __maxnreg__(88) bfly2_rotate_quant_kernel(const void* __restrict__ x,
                                                                  int64_t rows, int K,
                                                                  int8_t* __restrict__ q_out,
                                                                  float* __restrict__ scale_out,

@@ -28,6 +28,8 @@ cudaError_t launch_quantize_rows(const float* rot, int64_t rows, int K, int8_t* 
                                  cudaStream_t st);
 
 // gemm_i8.cu
+constexpr int kMaxPeers = 7;  // peer destinations of the column-split linear (8 GPUs per node)
+
 struct GemmI8Params {
   const int8_t* a;        // [M, K] row-major (token rows, rotated + quantised)
   const int8_t* b;        // [N, K] row-major (output channels)
@@ -39,6 +41,10 @@ struct GemmI8Params {
   int64_t M, N, K;
   int64_t ldo;
   int epilogue;
+  // Further destinations of the output, same layout as `out` (other GPUs' buffers mapped into
+  // this process): the epilogue stores every tile to `out` and to each of them.
+  void* peer_out[kMaxPeers];
+  int n_peer;
 };
 cudaError_t launch_gemm_i8(const GemmI8Params& p, cudaStream_t st);
 

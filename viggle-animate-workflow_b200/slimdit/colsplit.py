@@ -65,3 +65,143 @@ def int8_linear_colsplit(x: torch.Tensor, qweight_shard: torch.Tensor, wscales_s
                         convrot_groupsize=convrot_groupsize, bias=bias_shard)
     full = gather_columns(y, group=group, layout=layout)
     return full.reshape(*lead, -1) if layout == "rows" else full
+
+
+class _DeviceArray:
+    """Zero-copy view of library-owned device memory for torch.as_tensor (CUDA array interface)."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False),
+                                         "strides": None, "version": 3}
+
+
+class PeerColumnSplit:
+    """Column-split linear whose all-gather overlaps the GEMM over NVLink, writing straight
+    into every rank's output buffer (mapped into each process with CUDA IPC):
+
+      mode="dma"     the token rows are processed in chunks; each chunk's GEMM writes this
+                     rank's column block into the local output, and the copy engines push the
+                     finished chunk to every peer (2-D peer copies, one stream per peer) while
+                     the next chunk computes;
+      mode="stores"  the GEMM epilogue itself stores every tile into all ranks' outputs.
+
+    One instance per process (rank), created collectively; it owns the [m_max, n_full] bf16
+    output buffer this rank exposes to its peers (allocated by the library with a CUDA IPC
+    handle; plain peer mappings, no multicast object). A call synchronises the ranks twice with a
+    one-element NCCL all-reduce on the current stream: before the GEMM (every rank has
+    finished with the previous result) and after it (every rank's stores have landed). The
+    returned tensor is this rank's full output, valid until the next call.
+    """
+
+    def __init__(self, m_max: int, n_full: int, k: int, device=None, group=None, mode: str = "dma",
+                 chunk_rows: int = 4096):
+        import ctypes
+
+        from . import _native as nat
+
+        self._ct = ctypes
+        self._nat = nat
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("at most 8 ranks (GPUs of one node)")
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if mode not in ("dma", "stores"):
+            raise ValueError("mode must be 'dma' or 'stores'")
+        self.mode, self.chunk_rows = mode, max(1, chunk_rows)
+        self.m_max, self.n_full, self.k = m_max, n_full, k
+        self._copy_streams = [torch.cuda.Stream(device=self.device) for _ in range(max(0, self.world - 1))]
+        self.lib = nat.load()
+        self._own = None
+        self._opened = []
+        handle = ctypes.create_string_buffer(64)
+        own = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            nat.check(self.lib.slim_peer_buffer_alloc(m_max * n_full * 2, ctypes.byref(own), handle))
+        self._own = own.value
+        self.buf = torch.as_tensor(_DeviceArray(self._own, (m_max, n_full), "<i2"), device=self.device)
+        self.buf = self.buf.view(torch.bfloat16)
+        infos = [None] * self.world
+        dist.all_gather_object(infos, (self.rank, handle.raw), group=group)
+        self.ptrs = [0] * self.world
+        with torch.cuda.device(self.device):
+            for r, h in infos:
+                if r == self.rank:
+                    self.ptrs[r] = self._own
+                    continue
+                p = ctypes.c_void_p()
+                nat.check(self.lib.slim_peer_open(h, 0, ctypes.byref(p)))
+                self.ptrs[r] = p.value
+                self._opened.append((p.value, 0))
+        self.xq = torch.empty((m_max, k), dtype=torch.int8, device=self.device)
+        self.sx = torch.empty((m_max,), dtype=torch.float32, device=self.device)
+        self._flag = torch.zeros((1,), dtype=torch.float32, device=self.device)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (collective: every rank calls it before
+        tearing down; tensors returned by earlier calls are invalid afterwards)."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p, off in self._opened:
+                self._nat.check(self.lib.slim_peer_close(p, off))
+            self._opened = []
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)  # every peer has unmapped this rank's buffer
+            if self._own is not None:
+                self.buf = None
+                self._nat.check(self.lib.slim_peer_buffer_free(self._own))
+                self._own = None
+
+    def __call__(self, x: torch.Tensor, qweight_shard: torch.Tensor, wscales_shard: torch.Tensor,
+                 bias_shard: torch.Tensor | None = None, epilogue: str | None = None) -> torch.Tensor:
+        from . import ops
+
+        nat = self._nat
+        if x.dim() != 2 or x.shape[0] > self.m_max or x.shape[1] != self.k:
+            raise ValueError(f"x must be [<= {self.m_max}, {self.k}], got {tuple(x.shape)}")
+        if x.dtype not in ops._DT or not x.is_cuda:
+            raise TypeError("x must be a bf16/f16/f32 CUDA tensor")
+        m = x.shape[0]
+        nl = qweight_shard.shape[0]
+        if nl * self.world != self.n_full:
+            raise ValueError(f"shard of {nl} rows x {self.world} ranks != {self.n_full} output features")
+        x = x.contiguous()
+        sw = ops._vec(wscales_shard, nl, torch.float32, self.device, "wscales_shard")
+        b = ops._vec(bias_shard, nl, torch.bfloat16, self.device, "bias_shard")
+        col0 = self.rank * nl * 2  # bytes
+        peers = [r for r in range(self.world) if r != self.rank]
+        cur = torch.cuda.current_stream(self.device)
+        dist.all_reduce(self._flag, group=self.group)  # every rank is done with the previous result
+        with torch.cuda.device(self.device):
+            if self.mode == "stores":
+                outs = [self.ptrs[self.rank] + col0] + [self.ptrs[r] + col0 for r in peers]
+                self._linear(x, qweight_shard, sw, b, outs, 0, m, nl, epilogue, cur)
+            else:
+                pitch = self.n_full * 2
+                events = []
+                for r0 in range(0, m, self.chunk_rows):
+                    rows = min(self.chunk_rows, m - r0)
+                    self._linear(x, qweight_shard, sw, b, [self.ptrs[self.rank] + col0], r0, rows, nl, epilogue, cur)
+                    ev = torch.cuda.Event()
+                    ev.record(cur)
+                    events.append(ev)
+                    off = r0 * pitch + col0
+                    for s, r in zip(self._copy_streams, peers):
+                        s.wait_event(ev)
+                        nat.check(self.lib.slim_copy_2d(self.ptrs[r] + off, pitch, self.ptrs[self.rank] + off, pitch,
+                                                        nl * 2, rows, s.cuda_stream))
+                for s in self._copy_streams:
+                    cur.wait_stream(s)
+        dist.all_reduce(self._flag, group=self.group)  # every rank's data has landed
+        return self.buf[:m]
+
+    def _linear(self, x, qw, sw, b, outs, r0, rows, nl, epilogue, stream):
+        from . import ops
+
+        arr = (self._ct.c_void_p * len(outs))(*[o + r0 * self.n_full * 2 for o in outs])
+        self._nat.check(self.lib.slim_int8_linear_colsplit(
+            x.data_ptr() + r0 * self.k * x.element_size(), ops._DT[x.dtype], qw.data_ptr(), sw.data_ptr(), ops._ptr(b),
+            arr, len(outs), self.n_full, self.xq.data_ptr() + r0 * self.k, self.sx.data_ptr() + r0 * 4, rows, nl,
+            self.k, 256, ops._EPI[epilogue], stream.cuda_stream))
