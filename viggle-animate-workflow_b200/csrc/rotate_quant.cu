@@ -77,35 +77,57 @@ __device__ __forceinline__ float canon_zero(float v) { return v == 0.0f ? 0.0f :
 template <int ORDER_KIND>
 __device__ __forceinline__ float ref_rotate_one(const float* __restrict__ xs, int j);
 
-// G >= 5: one sequential chain. k = 16*b + l; the sign factorises as sigma(j, b) * lam(j, l).
-// The accumulator is carried as sigma_b * acc so the inner 16 steps are fma(x, lam_l, acc)
-// (exact product, one rounding); at a block change it is multiplied by sigma_b*sigma_{b-1}
-// (an exact sign flip). fl(s*a + s*t) = s*fl(a + t) keeps this identical to the plain chain.
-template <>
-__device__ __forceinline__ float ref_rotate_one<0>(const float* __restrict__ xs, int j) {
-  const int j0 = j & 3, j1 = (j >> 2) & 3, j2 = (j >> 4) & 3, j3 = (j >> 6) & 3;
+// G >= 5: one sequential chain per output over k = 0..255, k = 16*b + l. The sign factorises
+// as sigma(j, b) * lam(j, l); the accumulator is carried as sigma_b * acc so each step is one
+// fma(x, lam_l, acc) (exact product, one rounding), and at a block change it is multiplied by
+// sigma_b*sigma_{b-1} (an exact sign flip): fl(s*a + s*t) = s*fl(a + t) keeps this identical
+// to the plain chain.
+// Four outputs at once: j, j+64, j+128, j+192 (j < 64) share the base-4 digits j0..j2,
+// so they share lam(l) and the digit-2 factor h4(j2, b&3) of the block sign; they differ only
+// in the digit-3 factor H4[i][b>>2], i = 0..3, which is constant over each quad of blocks.
+// Each accumulator is carried as (its block sign) * acc, so every step is one
+// fma(x, lam_l, acc); at a block change all four are multiplied by
+// h4(j2,b&3)*h4(j2,(b-1)&3), and at a quad change output i additionally by
+// H4[i][B]*H4[i][B-1] (compile-time +-1). Same roundings as the plain chain; the x loads and
+// lam are shared by four independent chains.
+__device__ __forceinline__ void ref_rotate_four0(const float* __restrict__ xs, int j, float (&y)[4]) {
+  const int j0 = j & 3, j1 = (j >> 2) & 3, j2 = (j >> 4) & 3;
   float lam[16];
 #pragma unroll
   for (int l = 0; l < 16; ++l) lam[l] = h4sign(j1, l >> 2) * h4sign(j0, l & 3);
-  float sig[16];
+  float s2[4];
 #pragma unroll
-  for (int b = 0; b < 16; ++b) sig[b] = h4sign(j3, b >> 2) * h4sign(j2, b & 3);
+  for (int c = 0; c < 4; ++c) s2[c] = h4sign(j2, c);
   const float4* x4 = reinterpret_cast<const float4*>(xs);
-  float acc = 0.0f;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
   for (int b = 0; b < 16; ++b) {
-    if (b > 0) acc *= sig[b] * sig[b - 1];
+    if (b > 0) {
+      const float f = s2[b & 3] * s2[(b - 1) & 3];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float g = f;
+        if ((b & 3) == 0 && h4sign(i, b >> 2) != h4sign(i, (b >> 2) - 1)) g = -g;
+        acc[i] *= g;
+      }
+    }
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const float4 v = x4[b * 4 + q];
-      acc = __fmaf_rn(v.x, lam[4 * q + 0], acc);
-      acc = __fmaf_rn(v.y, lam[4 * q + 1], acc);
-      acc = __fmaf_rn(v.z, lam[4 * q + 2], acc);
-      acc = __fmaf_rn(v.w, lam[4 * q + 3], acc);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[i] = __fmaf_rn(v.x, lam[4 * q + 0], acc[i]);
+        acc[i] = __fmaf_rn(v.y, lam[4 * q + 1], acc[i]);
+        acc[i] = __fmaf_rn(v.z, lam[4 * q + 2], acc[i]);
+        acc[i] = __fmaf_rn(v.w, lam[4 * q + 3], acc[i]);
+      }
     }
   }
-  acc *= sig[15];
-  return canon_zero(acc * 0.0625f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float last = s2[3] * h4sign(i, 3);  // the block sign of block 15 for output i
+    y[i] = canon_zero(acc[i] * last * 0.0625f);
+  }
 }
 
 // 2 <= G <= 4: 16 chains over k mod 16 (k = 16*t + l), then the pairwise tree.
@@ -244,6 +266,76 @@ __global__ void __launch_bounds__(256) ref_rotate_kernel(const void* __restrict_
       if (j == 0) scale_out[row] = scale;
       // 4 codes per thread per step: coalesced 4-byte stores.
       for (int c = 4 * j; c < K; c += 4 * 256) {
+        const float4 v = *reinterpret_cast<const float4*>(rowbuf + c);
+        char4 o;
+        o.x = quant_code(v.x, scale);
+        o.y = quant_code(v.y, scale);
+        o.z = quant_code(v.z, scale);
+        o.w = quant_code(v.w, scale);
+        *reinterpret_cast<char4*>(q_out + base + c) = o;
+      }
+    }
+  }
+}
+
+// Reference order for G >= 5 with four outputs per thread: one CTA of 256 threads per row
+// handles four groups at a time (thread t: group slot t/64, outputs t%64 + 64*i).
+template <int DT, bool DEQ, int MODE>
+__global__ void __launch_bounds__(256) ref_rotate4_kernel(const void* __restrict__ x,
+                                                          const float* __restrict__ deq_scale,
+                                                          int64_t rows, int K,
+                                                          float* __restrict__ rot_out,
+                                                          int8_t* __restrict__ q_out,
+                                                          float* __restrict__ scale_out) {
+  extern __shared__ __align__(16) float smem_f[];
+  float* xs = smem_f;            // 4 groups x 256 inputs
+  float* red = smem_f + 1024;    // 32 warp partials
+  float* rowbuf = smem_f + 1056; // K rotated values (MODE 1)
+  const int t = threadIdx.x;
+  const int slot = t >> 6, j = t & 63;
+  const int groups = K >> 8;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int64_t base = row * static_cast<int64_t>(K);
+    float rs = 1.0f;
+    if (DEQ) rs = __ldg(deq_scale + row);
+    float amax = 0.0f;
+    for (int g0 = 0; g0 < groups; g0 += 4) {
+      const int ng = min(4, groups - g0);
+      __syncthreads();  // previous groups' inputs fully consumed
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int idx = e * 256 + t;  // input idx of the 4-group window
+        if (idx < ng * 256) {
+          float v;
+          if (DEQ) {
+            v = static_cast<float>(__ldg(static_cast<const int8_t*>(x) + base + g0 * 256 + idx)) * rs;
+          } else {
+            v = Loader<DT>::at(x, base + g0 * 256 + idx);
+          }
+          xs[idx] = v;
+        }
+      }
+      __syncthreads();
+      if (slot < ng) {
+        float y[4];
+        ref_rotate_four0(xs + slot * 256, j, y);
+        const int64_t o = base + (g0 + slot) * 256 + j;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (MODE == 0) {
+            rot_out[o + 64 * i] = y[i];
+          } else {
+            rowbuf[(g0 + slot) * 256 + j + 64 * i] = y[i];
+            amax = fmaxf(amax, fabsf(y[i]));
+          }
+        }
+      }
+    }
+    if (MODE == 1) {
+      const float m = block_max(amax, red);  // includes the barrier making rowbuf visible
+      const float scale = row_scale_from_absmax(m);
+      if (t == 0) scale_out[row] = scale;
+      for (int c = 4 * t; c < K; c += 4 * 256) {
         const float4 v = *reinterpret_cast<const float4*>(rowbuf + c);
         char4 o;
         o.x = quant_code(v.x, scale);
@@ -543,12 +635,25 @@ template <int DT, bool DEQ, int MODE>
 static cudaError_t launch_ref(const void* x, const float* deq_scale, int64_t rows, int K,
                               float* rot_out, int8_t* q, float* scale, cudaStream_t st) {
   const int groups = K >> 8;
-  const size_t smem = (288 + (MODE == 1 ? static_cast<size_t>(K) : 0)) * sizeof(float);
   const int kind = groups >= 5 ? 0 : (groups >= 2 ? 1 : 2);
+  if (kind == 0) {
+    const size_t smem4 = (1056 + (MODE == 1 ? static_cast<size_t>(K) : 0)) * sizeof(float);
+    auto fn4 = ref_rotate4_kernel<DT, DEQ, MODE>;
+    if (smem4 > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(fn4, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem4));
+      if (e != cudaSuccess) return e;
+    }
+    int per_sm = 1;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn4, 256, smem4);
+    if (e != cudaSuccess) return e;
+    const int grid4 = grid_for_rows(rows, per_sm < 1 ? 1 : per_sm);
+    fn4<<<grid4, 256, smem4, st>>>(x, deq_scale, rows, K, rot_out, q, scale);
+    return cudaGetLastError();
+  }
+  const size_t smem = (288 + (MODE == 1 ? static_cast<size_t>(K) : 0)) * sizeof(float);
   const int grid = grid_for_rows(rows, 8);
   void (*fn)(const void*, const float*, int64_t, int, float*, int8_t*, float*) =
-      kind == 0 ? ref_rotate_kernel<DT, DEQ, MODE, 0>
-                : (kind == 1 ? ref_rotate_kernel<DT, DEQ, MODE, 1> : ref_rotate_kernel<DT, DEQ, MODE, 2>);
+      kind == 1 ? ref_rotate_kernel<DT, DEQ, MODE, 1> : ref_rotate_kernel<DT, DEQ, MODE, 2>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
