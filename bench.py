@@ -285,6 +285,56 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
     del xq, sx, h, hq, sh, y, qu, qd
     torch.cuda.empty_cache()
 
+    # ---- the real MiniMax-H3 linears (tools/bench_int8.py:23-28) at the same token count:
+    # qkv, out_proj, and the SwiGLU FFN (fc1 with the fused SwiGLU epilogue, requant, fc2)
+    mm = (FFN_TOKENS + world - 1) // world
+    xh = (torch.randn((mm, 5376), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    xo = (torch.randn((mm, 7168), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+
+    def qweight(n, k):
+        w = (torch.randn((n, k), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        q, s_ = ops.rotate_quant(w, order="butterfly")
+        return q, s_.reshape(-1).contiguous()
+
+    shapes = {"qkv": (21504, 5376, xh), "out_proj": (5376, 7168, xo)}
+    res = {}
+    for name, (n_, k_, xin) in shapes.items():
+        q, s_ = qweight(n_, k_)
+        for _ in range(2):
+            ops.int8_linear(xin, q, s_)
+        torch.cuda.synchronize(dev)
+        barrier()
+        a.record(stream)
+        for _ in range(steps):
+            ops.int8_linear(xin, q, s_)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = reduce_max(a.elapsed_time(b) / steps)
+        res[name] = {"M": mm, "N": n_, "K": k_, "ms": round(ms, 4),
+                     "TOPS": round(world * 2.0 * mm * n_ * k_ / (ms * 1e-3) / 1e12, 1)}
+        del q, s_
+    q1, s1 = qweight(28672, 5376)
+    q1, s1, _ = ops.swiglu_interleave(q1, s1)
+    q2, s2 = qweight(5376, 14336)
+    for _ in range(2):
+        ops.ffn_swiglu_int8(xh, q1, s1, q2, s2)
+    torch.cuda.synchronize(dev)
+    barrier()
+    a.record(stream)
+    for _ in range(steps):
+        ops.ffn_swiglu_int8(xh, q1, s1, q2, s2)
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = reduce_max(a.elapsed_time(b) / steps)
+    ffn_ops = 2.0 * FFN_TOKENS * 28672 * 5376 + 2.0 * FFN_TOKENS * 5376 * 14336
+    res["ffn_swiglu"] = {"M": mm, "fc1": [28672, 5376], "fc2": [5376, 14336], "ms": round(ms, 4),
+                         "TOPS": round(ffn_ops / (ms * 1e-3) / 1e12, 1)}
+    out["minimax_h3"] = {"workload": f"MiniMax-H3 linears at {FFN_TOKENS} tokens (split over the ranks): qkv, "
+                                     "out_proj, and the FFN fc1 -> fused SwiGLU -> rotate+requant -> fc2",
+                         "shapes": res, "unit": "TOPS", "scaling": "strong", "steps": steps}
+    del xh, xo, q1, s1, q2, s2
+    torch.cuda.empty_cache()
+
     # ---- config 3: NVFP4 up-proj (rotate + per-token NVFP4 of x, block-scaled FP4 GEMM)
     wu = (torch.randn((FFN_F, FFN_H), generator=g, device=dev) * 0.02).to(torch.bfloat16)
     pw, pws, pwg = ops.nvfp4_pack(wu)

@@ -44,7 +44,12 @@ enum slim_status {
 
 enum slim_dtype { SLIM_F32 = 0, SLIM_BF16 = 1, SLIM_F16 = 2 };
 enum slim_order { SLIM_ORDER_REFERENCE = 0, SLIM_ORDER_BUTTERFLY = 1 };
-enum slim_epilogue { SLIM_EPI_SCALE_BIAS = 0, SLIM_EPI_GELU_TANH = 1 };
+/* SLIM_EPI_SWIGLU (INT8 GEMM only): the weight's rows are interleaved per 256-row tile, 128
+ * "up" rows then the 128 matching "gate" rows (slim_swiglu_interleave order); the output
+ * has N/2 columns, out[m, t*128 + i] = bf16(up * bf16(silu(gate))) with up and gate the bf16
+ * linear outputs of rows 256t + i and 256t + 128 + i: ComfyUI's swiglu ([up; gate],
+ * slimdit/mapping.py:96-97) on the bf16 output of the fc1 linear, fused. N % 256 == 0. */
+enum slim_epilogue { SLIM_EPI_SCALE_BIAS = 0, SLIM_EPI_GELU_TANH = 1, SLIM_EPI_SWIGLU = 2 };
 
 /* ABI version (SLIM_ABI_VERSION). */
 int slim_version(void);

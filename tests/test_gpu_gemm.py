@@ -188,3 +188,43 @@ def test_int8_linear_host_pipelined_equals_device_call(cuda, m, chunk, pinned):
     torch.cuda.current_stream(cuda).synchronize()
     ref = ops.int8_linear(xh.to(cuda), qw_d, sw_d, bias=bias.to(cuda)).cpu()
     assert y.device.type == "cpu" and torch.equal(y, ref)
+
+
+def test_swiglu_epilogue_and_minimax_ffn(cuda):
+    """fc1 with the fused SwiGLU epilogue (weights in swiglu_interleave order) against the
+    plain linear's bf16 up/gate outputs followed by bf16(up * bf16(silu(gate))) in fp32; then
+    the whole FFN (fc1 -> SwiGLU -> rotate + requant -> fc2)."""
+    from slimdit import ops
+    from slimdit.int8 import quantize_convrot_weight
+    m, hdim, f = 300, 512, 1024
+    x = synthetic.activations(m, hdim, seed=41)
+    w1 = synthetic.weight(2 * f, hdim, seed=42)
+    w2 = synthetic.weight(hdim, f, seed=43)
+    b1 = synthetic.bf16_round_f32(np.random.default_rng(44).standard_normal(2 * f).astype(np.float32) * 0.02)
+    q1, s1 = quantize_convrot_weight(w1)
+    q2, s2 = quantize_convrot_weight(w2)
+    xt = torch.from_numpy(x).to(cuda).to(torch.bfloat16)
+    q1d, s1d = torch.from_numpy(q1).to(cuda), torch.from_numpy(s1).to(cuda)
+    b1d = torch.from_numpy(b1).to(cuda).to(torch.bfloat16)
+    q2d, s2d = torch.from_numpy(q2).to(cuda), torch.from_numpy(s2).to(cuda)
+    qi, si, bi = ops.swiglu_interleave(q1d, s1d, b1d)
+    qi_h, si_h = qi.cpu().numpy(), si.cpu().numpy()
+    for t in range(2 * f // 256):
+        assert np.array_equal(qi_h[256 * t:256 * t + 128], q1[128 * t:128 * t + 128])
+        assert np.array_equal(qi_h[256 * t + 128:256 * t + 256], q1[f + 128 * t:f + 128 * t + 128])
+        assert np.array_equal(si_h[256 * t:256 * t + 128], s1.reshape(-1)[128 * t:128 * t + 128])
+    lin = ops.int8_linear(xt, q1d, s1d, bias=b1d).float().cpu().numpy()
+    up, gate = lin[:, :f].astype(np.float32), lin[:, f:].astype(np.float32)
+    silu = oracle.bf16_round((gate / (np.float32(1.0) + np.exp(-gate))).astype(np.float32))
+    ref = oracle.bf16_round((up * silu).astype(np.float32))
+    y = ops.int8_linear(xt, qi, si, bias=bi, epilogue="swiglu")
+    assert y.shape == (m, f)
+    yv = y.float().cpu().numpy()
+    diff = np.abs(yv - ref)
+    assert np.all(diff <= oracle.bf16_ulp(ref) + 1e-30), "SwiGLU beyond 1 bf16 ulp"
+    assert (diff > 0).mean() < 1e-3  # only expf/np.exp last-bit differences may remain
+    yf = ops.ffn_swiglu_int8(xt, qi, si, q2d, s2d, bi, None)
+    ref_f = ops.int8_linear(y, q2d, s2d)
+    assert torch.equal(yf, ref_f)
+    with pytest.raises(ValueError):  # rows not a multiple of 256
+        ops.swiglu_interleave(q1d[:384], s1d[:384])

@@ -184,13 +184,19 @@ int slim_dequant_i8(const int8_t* q, const float* scale, int64_t rows, int64_t K
   return SLIM_OK;
 }
 
+// Output row pitch: N columns, or N/2 for the SwiGLU epilogue (one output per up/gate pair).
+static int64_t out_pitch(int64_t N, int epilogue) { return epilogue == kEpiSwiGLU ? N / 2 : N; }
+
 static int gemm_checks(const int8_t* a, const int8_t* b, const float* sa, const float* sb, const void* bias,
                        const void* out, const int32_t* acc_dbg, int64_t M, int64_t N, int64_t K, int epilogue) {
   if (M < 0 || N <= 0 || K <= 0) return fail(SLIM_ERR_SHAPE, "bad GEMM shape M=%lld N=%lld K=%lld", static_cast<long long>(M), static_cast<long long>(N), static_cast<long long>(K));
   if (K % 16 != 0) return fail(SLIM_ERR_SHAPE, "K=%lld must be a multiple of 16", static_cast<long long>(K));
   if (N % 8 != 0) return fail(SLIM_ERR_SHAPE, "N=%lld must be a multiple of 8", static_cast<long long>(N));
   if (M > (int64_t{1} << 31) || N > (int64_t{1} << 31)) return fail(SLIM_ERR_SHAPE, "GEMM dimension too large");
-  if (epilogue != kEpiScaleBias && epilogue != kEpiGeluTanh) return fail(SLIM_ERR_DTYPE, "unknown epilogue %d", epilogue);
+  if (epilogue != kEpiScaleBias && epilogue != kEpiGeluTanh && epilogue != kEpiSwiGLU)
+    return fail(SLIM_ERR_DTYPE, "unknown epilogue %d", epilogue);
+  if (epilogue == kEpiSwiGLU && (N % 256 != 0 || acc_dbg != nullptr))
+    return fail(SLIM_ERR_SHAPE, "the SwiGLU epilogue needs N %% 256 == 0 (interleaved up/gate rows) and no accumulator copy");
   if (M == 0) return SLIM_OK;  // empty problem: nothing is read or written
   if (a == nullptr || b == nullptr || sa == nullptr || sb == nullptr || out == nullptr) return fail(SLIM_ERR_NULL, "a/b/sa/sb/out is NULL");
   if (!aligned16(a) || !aligned16(b) || !aligned16(sb) || !aligned16(out) || (bias != nullptr && !aligned16(bias)) ||
@@ -205,7 +211,7 @@ int slim_gemm_i8(const int8_t* a, const int8_t* b, const float* sa, const float*
   if ((rc = gemm_checks(a, b, sa, sb, bias, out, acc_dbg, M, N, K, epilogue)) != SLIM_OK) return rc;
   if (M == 0) return SLIM_OK;
   if ((rc = check_arch()) != SLIM_OK) return rc;
-  GemmI8Params p{a, b, sa, sb, bias, out, acc_dbg, M, N, K, N, epilogue};
+  GemmI8Params p{a, b, sa, sb, bias, out, acc_dbg, M, N, K, out_pitch(N, epilogue), epilogue};
   cudaError_t e = launch_gemm_i8(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
   note_launch();
@@ -228,7 +234,7 @@ int slim_int8_linear(const void* x, int x_dtype, const int8_t* qw, const float* 
   cudaError_t e = launch_bfly_rotate_quant(x, x_dtype, M, static_cast<int>(K), xq_ws, sx_ws, nullptr, st);
   if (e != cudaSuccess) return cuda_fail(e, "activation quant launch");
   note_launch();
-  GemmI8Params p{xq_ws, qw, sx_ws, sw, bias, out, nullptr, M, N, K, N, epilogue};
+  GemmI8Params p{xq_ws, qw, sx_ws, sw, bias, out, nullptr, M, N, K, out_pitch(N, epilogue), epilogue};
   e = launch_gemm_i8(p, st);
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
   note_launch();
@@ -303,6 +309,7 @@ int slim_int8_linear_colsplit(const void* x, int x_dtype, const int8_t* qw, cons
   if ((rc = check_dtype(x_dtype)) != SLIM_OK) return rc;
   if (K > 16384) return fail(SLIM_ERR_SHAPE, "in_features above 16384 not supported by the activation quantiser");
   if ((rc = gemm_checks(xq_ws, qw, sx_ws, sw, bias, outs[0], nullptr, M, N, K, epilogue)) != SLIM_OK) return rc;
+  if (epilogue == kEpiSwiGLU) return fail(SLIM_ERR_DTYPE, "the column-split linear does not take the SwiGLU epilogue");
   if (M == 0) return SLIM_OK;
   if (x == nullptr) return fail(SLIM_ERR_NULL, "x is NULL");
   if (!aligned16(x)) return fail(SLIM_ERR_ALIGN, "x must be 16-byte aligned");

@@ -24,7 +24,8 @@ static int nvfp4_gemm_checks(const uint8_t* a, const uint8_t* a_sf, const float*
   if (K % 64 != 0) return fail(SLIM_ERR_SHAPE, "K=%lld must be a multiple of 64", static_cast<long long>(K));
   if (N % 128 != 0) return fail(SLIM_ERR_SHAPE, "N=%lld must be a multiple of 128 (NVFP4 weight tiling)", static_cast<long long>(N));
   if (M > (int64_t{1} << 31) || N > (int64_t{1} << 31)) return fail(SLIM_ERR_SHAPE, "GEMM dimension too large");
-  if (epilogue != kEpiScaleBias && epilogue != kEpiGeluTanh) return fail(SLIM_ERR_DTYPE, "unknown epilogue %d", epilogue);
+  if (epilogue != kEpiScaleBias && epilogue != kEpiGeluTanh)
+    return fail(SLIM_ERR_DTYPE, "unknown epilogue %d (the NVFP4 GEMM takes scale+bias or GELU-tanh)", epilogue);
   if (M == 0) return SLIM_OK;
   if (a == nullptr || a_sf == nullptr || a_scale == nullptr || b == nullptr || b_sf == nullptr || b_scale == nullptr ||
       out == nullptr)

@@ -81,11 +81,73 @@ __device__ __forceinline__ float bf16_round(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));
 }
 
+// Eight scale/bias-applied outputs y = bf16(acc * sa * sb[n] + bias[n]) as fp32, columns n0..n0+7.
+__device__ __forceinline__ void linear8(const GemmI8Params& p, const uint32_t* r, float sam, int64_t n0, float (&y)[8]) {
+  const __nv_bfloat16* bias = static_cast<const __nv_bfloat16*>(p.bias);
+  const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.sb + n0));
+  const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + 4));
+  const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+  float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (bias != nullptr) {
+    const uint4 bu = __ldg(reinterpret_cast<const uint4*>(bias + n0));
+    const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      bv[2 * e] = __uint_as_float(bw[e] << 16);
+      bv[2 * e + 1] = __uint_as_float(bw[e] & 0xffff0000u);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    y[e] = bf16_round(__fmaf_rn(static_cast<float>(static_cast<int>(r[e])), sam * sv[e], bv[e]));
+}
+
+// SwiGLU epilogue: the weight rows are interleaved per 256-row tile (128 "up" rows, then the 128
+// matching "gate" rows), so the tile's columns [0,128) and [128,256) pair up; the output
+// column n_base/2 + i gets bf16(up * bf16(silu(gate))), with up and gate the bf16 linear
+// outputs: the roundings of running the linear in bf16 and then ComfyUI's swiglu on its output.
+__device__ __forceinline__ void epilogue_rows_swiglu(const GemmI8Params& p, uint32_t tbase, int64_t m, bool row_ok,
+                                                     float sam, int64_t n_base) {
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+  const int64_t o_base = n_base / 2;
+#pragma unroll 1
+  for (int c = 0; c < BN / 64; ++c) {
+    uint32_t ru[32], rg[32];
+    tmem_ld_32x32b_x32(tbase + c * 32, ru);
+    tmem_ld_32x32b_x32(tbase + BN / 2 + c * 32, rg);
+    tmem_ld_wait();
+    const int64_t nu = n_base + c * 32, ng = n_base + BN / 2 + c * 32;
+    if (!row_ok || nu >= p.N) continue;
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      float up[8], g[8];
+      linear8(p, ru + j, sam, nu + j, up);
+      linear8(p, rg + j, sam, ng + j, g);
+      float y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float sl = bf16_round(__fdiv_rn(g[e], __fadd_rn(1.0f, expf(-g[e]))));
+        y[e] = __fmul_rn(up[e], sl);
+      }
+      uint4 o;
+      o.x = pack_bf16x2(y[0], y[1]);
+      o.y = pack_bf16x2(y[2], y[3]);
+      o.z = pack_bf16x2(y[4], y[5]);
+      o.w = pack_bf16x2(y[6], y[7]);
+      *reinterpret_cast<uint4*>(out + m * p.ldo + o_base + c * 32 + j) = o;
+    }
+  }
+}
+
 // One accumulator tile row-slice: this thread's row m (TMEM lane), 256 columns from n_base,
 // read 32 columns at a time; scale/bias(/GELU) in fp32, bf16 stores, optional int32 copy.
 // All 32 lanes of the warp must call it (tcgen05.ld is warp-collective).
 __device__ __forceinline__ void epilogue_rows(const GemmI8Params& p, uint32_t tbase, int64_t m, bool row_ok,
                                               float sam, int64_t n_base) {
+  if (p.epilogue == kEpiSwiGLU) {
+    epilogue_rows_swiglu(p, tbase, m, row_ok, sam, n_base);
+    return;
+  }
   const __nv_bfloat16* bias = static_cast<const __nv_bfloat16*>(p.bias);
   __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
 #pragma unroll 1

@@ -85,7 +85,7 @@ extern "C" int slim_int8_linear_noalloc(const void* x, int x_dtype, const int8_t
   cudaError_t e = launch_bfly_rotate_quant(x, x_dtype, M, static_cast<int>(K), xq, sx, nullptr, st);
   if (e != cudaSuccess) return cuda_fail(e, "activation quant launch");
   note_launch();
-  GemmI8Params p{xq, qw, sx, sw, bias, out, nullptr, M, N, K, N, epilogue};
+  GemmI8Params p{xq, qw, sx, sw, bias, out, nullptr, M, N, K, out_pitch(N, epilogue), epilogue};
   e = launch_gemm_i8(p, st);
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
   note_launch();

@@ -13,6 +13,7 @@ enum DType : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
 enum Epilogue : int {
   kEpiScaleBias = 0,   // y = bf16(acc * sa[m] * sb[n] + bias[n])
   kEpiGeluTanh = 1,    // y = bf16(gelu_tanh(float(bf16(acc * sa[m] * sb[n] + bias[n]))))
+  kEpiSwiGLU = 2,      // rows interleaved per 256 (128 up, 128 gate): y[m, n/2 + i] = bf16(up * bf16(silu(gate)))
 };
 
 // rotate_quant.cu

@@ -35,7 +35,7 @@ SLIM_ERR_NULL = -7
 
 F32, BF16, F16 = 0, 1, 2
 ORDER_REFERENCE, ORDER_BUTTERFLY = 0, 1
-EPI_SCALE_BIAS, EPI_GELU_TANH = 0, 1
+EPI_SCALE_BIAS, EPI_GELU_TANH, EPI_SWIGLU = 0, 1, 2
 
 
 class NativeUnavailable(RuntimeError):

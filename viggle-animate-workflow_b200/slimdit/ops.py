@@ -11,6 +11,8 @@ computation runs in libslimdit_b200.so).
 * ``int8_linear``   the convrot W8A8 linear, same call shape as the runtime op the reference
                     benchmarks (``comfy_kitchen.int8_linear``, tools/bench_int8.py:65-68)
 * ``ffn_int8``      up-proj -> GELU-tanh -> rotate + requant -> down-proj
+* ``swiglu_interleave`` / ``ffn_swiglu_int8``  the MiniMax-H3 FFN: fc1 with a fused SwiGLU
+                    epilogue, rotate + requant, fc2
 * ``int8_linear_host``  the linear on host-resident activations, copies and compute of row
                     chunks overlapped on three streams
 * ``nvfp4_pack`` / ``nvfp4_quantize_act`` / ``nvfp4_dequantize`` / ``nvfp4_error`` /
@@ -25,7 +27,8 @@ from . import _native as nat
 
 _DT = {torch.float32: nat.F32, torch.bfloat16: nat.BF16, torch.float16: nat.F16}
 _ORDERS = {"reference": nat.ORDER_REFERENCE, "butterfly": nat.ORDER_BUTTERFLY}
-_EPI = {None: nat.EPI_SCALE_BIAS, "none": nat.EPI_SCALE_BIAS, "gelu_tanh": nat.EPI_GELU_TANH}
+_EPI = {None: nat.EPI_SCALE_BIAS, "none": nat.EPI_SCALE_BIAS, "gelu_tanh": nat.EPI_GELU_TANH,
+        "swiglu": nat.EPI_SWIGLU}
 
 
 def _cuda2d(t: torch.Tensor, name: str) -> torch.Tensor:
@@ -132,10 +135,11 @@ def gemm_i8(a: torch.Tensor, b: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor
     sa = _vec(sa, m, torch.float32, dev, "sa")
     sb = _vec(sb, n, torch.float32, dev, "sb")
     bias = _vec(bias, n, torch.bfloat16, dev, "bias")
+    n_out = n // 2 if epilogue == "swiglu" else n
     if out is None:
-        out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
-    elif out.shape != (m, n) or out.dtype != torch.bfloat16 or not out.is_contiguous():
-        raise ValueError("out must be a contiguous bf16 [M, N] tensor")
+        out = torch.empty((m, n_out), dtype=torch.bfloat16, device=dev)
+    elif out.shape != (m, n_out) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous bf16 [{m}, {n_out}] tensor")
     acc = torch.empty((m, n), dtype=torch.int32, device=dev) if return_acc else None
     with torch.cuda.device(dev):
         nat.check(nat.load().slim_gemm_i8(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(), _ptr(bias),
@@ -168,7 +172,8 @@ def int8_linear(x: torch.Tensor, qweight: torch.Tensor, wscales: torch.Tensor, c
     dev = x2.device
     sw = _vec(wscales, n, torch.float32, dev, "wscales")
     b = _vec(bias, n, torch.bfloat16, dev, "bias")
-    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    n_out = n // 2 if epilogue == "swiglu" else n
+    out = torch.empty((m, n_out), dtype=torch.bfloat16, device=dev)
     if convrot:
         xq = torch.empty((m, k), dtype=torch.int8, device=dev)
         sx = torch.empty((m,), dtype=torch.float32, device=dev)
@@ -177,9 +182,11 @@ def int8_linear(x: torch.Tensor, qweight: torch.Tensor, wscales: torch.Tensor, c
                                                   _ptr(b), out.data_ptr(), xq.data_ptr(), sx.data_ptr(), m, n, k,
                                                   convrot_groupsize, _EPI[epilogue], _stream(x2)))
     else:
+        if epilogue == "swiglu":
+            raise ValueError("the SwiGLU epilogue needs convrot=True")
         xq, sx = quantize_rows(x2.float())
         gemm_i8(xq, qweight, sx, sw, b, epilogue=epilogue, out=out)
-    out = out.reshape(*lead, n)
+    out = out.reshape(*lead, n_out)
     return out if out_dtype == torch.bfloat16 else out.to(out_dtype)
 
 
@@ -229,8 +236,8 @@ def int8_linear_host(x: torch.Tensor, qweight: torch.Tensor, wscales: torch.Tens
     n = qweight.shape[0]
     if qweight.shape[1] != k:
         raise ValueError(f"in_features mismatch: x [..., {k}] vs qweight {tuple(qweight.shape)}")
-    if epilogue not in _EPI:
-        raise ValueError(f"epilogue must be one of {sorted(str(e) for e in _EPI)}")
+    if epilogue not in _EPI or epilogue == "swiglu":
+        raise ValueError("epilogue must be None, 'none' or 'gelu_tanh' for the host-memory linear")
     if chunk_rows <= 0:
         raise ValueError("chunk_rows must be positive")
     sw = _vec(wscales, n, torch.float32, dev, "wscales")
@@ -283,6 +290,48 @@ def int8_linear_host(x: torch.Tensor, qweight: torch.Tensor, wscales: torch.Tens
         cur.wait_stream(s_cmp)
         cur.wait_stream(s_h2d)
     return out
+
+
+def swiglu_interleave(qweight: torch.Tensor, wscales: torch.Tensor, bias: torch.Tensor | None = None):
+    """Reorder a gated projection's rows [up; gate] (N = 2F rows, ComfyUI's swiglu order,
+    slimdit/mapping.py:96-97) into the SwiGLU epilogue's order: per 256-row tile, 128 up rows
+    then the 128 matching gate rows. Pure data movement (2-D copies on the current stream);
+    returns (qweight, wscales [N], bias [N] or None)."""
+    qweight = _cuda2d(qweight, "qweight")
+    n, k = qweight.shape
+    if n % 256:
+        raise ValueError(f"the gated projection needs a multiple of 256 rows, got {n}")
+    dev = qweight.device
+    f = n // 2
+    sw = _vec(wscales, n, torch.float32, dev, "wscales")
+    b = _vec(bias, n, torch.bfloat16, dev, "bias")
+    lib = nat.load()
+    st = _stream(qweight)
+    outs = []
+    with torch.cuda.device(dev):
+        for t in (qweight, sw, b):
+            if t is None:
+                outs.append(None)
+                continue
+            row = (t.shape[1] if t.dim() == 2 else 1) * t.element_size()
+            dst = torch.empty_like(t)
+            for half in (0, 1):  # up rows -> first 128 of each tile, gate rows -> last 128
+                nat.check(lib.slim_copy_2d(dst.data_ptr() + half * 128 * row, 256 * row,
+                                           t.data_ptr() + half * f * row, 128 * row, 128 * row, f // 128, st))
+            outs.append(dst)
+    return outs[0], outs[1], outs[2]
+
+
+def ffn_swiglu_int8(x: torch.Tensor, w_fc1: torch.Tensor, s_fc1: torch.Tensor, w_fc2: torch.Tensor,
+                    s_fc2: torch.Tensor, b_fc1: torch.Tensor | None = None,
+                    b_fc2: torch.Tensor | None = None) -> torch.Tensor:
+    """The MiniMax-H3 FFN on the convrot linear: fc2(rotquant(swiglu(fc1(x)))).
+
+    w_fc1/s_fc1/b_fc1 are the gated projection in :func:`swiglu_interleave` order (prepare once
+    at load time); fc1's epilogue applies SwiGLU to its bf16 outputs and writes [M, F]; the
+    result is rotated and requantised per token for fc2."""
+    h = int8_linear(x, w_fc1, s_fc1, bias=b_fc1, epilogue="swiglu")
+    return int8_linear(h, w_fc2, s_fc2, bias=b_fc2)
 
 
 # ---------------------------------------------------------------- NVFP4
