@@ -214,6 +214,20 @@ int slim_nvfp4_linear(const void* x, int x_dtype, const uint8_t* qw, const uint8
                       uint8_t* xsf_ws, float* xs_ws, int64_t M, int64_t N, int64_t K,
                       int rotate, int epilogue, void* stream);
 
+/* ---------------------------------------------------------------- verification
+ * Relative-L2 building blocks of tools/verify_checkpoint.py (compare_reference /
+ * compare_official, tools/verify_checkpoint.py:81-152), reduced in fp64 on the GPU. Both add
+ * sum (a - b)^2 to out2[0] and sum b^2 to out2[1] (device fp64[2], not cleared). */
+
+/* INT8 rows in the rotated basis, a = fl32(qa * sa[row]), b = fl32(qb * sb[row]): the
+ * load_value(rotated=True) comparison (tools/verify_checkpoint.py:71-75). K % 16 == 0. */
+int slim_rel_l2_int8(const int8_t* qa, const float* sa, const int8_t* qb, const float* sb,
+                     int64_t rows, int64_t K, double* out2, void* stream);
+
+/* Two n-element tensors of SLIM_F32/BF16/F16, compared as fp32 values. */
+int slim_rel_l2(const void* a, int a_dtype, const void* b, int b_dtype, int64_t n,
+                double* out2, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

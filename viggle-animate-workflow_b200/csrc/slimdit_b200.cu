@@ -7,3 +7,4 @@
 #include "nvfp4_quant.cu"
 #include "gemm_nvf4.cu"
 #include "capi_nvfp4.cu"
+#include "verify.cu"
