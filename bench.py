@@ -473,17 +473,19 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
         gather_ms = reduce_max(sum(mids[i].elapsed_time(ends[i]) for i in range(steps)) / steps)
         out["colsplit_linear"] = {
             "workload": f"config-1 linear, W rows split {world} ways, x replicated, NCCL all-gather of "
-                        f"[{M},{nl}] bf16 blocks",
+                        f"[{M},{nl}] bf16 blocks ([G,M,N/G] layout)",
             "ms_per_step": round(ms, 4), "allgather_ms": round(gather_ms, 4),
             "value": round(OPS_PER_STEP / (ms * 1e-3) / 1e12, 1), "unit": "TOPS", "scaling": "strong",
             "allgather_busbw_gbs": round((world - 1) * M * nl * 2 / (gather_ms * 1e-3) / 1e9, 1), "steps": steps}
         del y_loc, blocks, xq, sx
         torch.cuda.empty_cache()
         # the same split with the all-gather inside the GEMM epilogue (peer stores over NVLink)
-        for mode, what in (("dma", "4096-row chunks, each pushed to every peer by the copy engines while the next "
-                                   "chunk computes"),
-                           ("stores", "the GEMM epilogue stores each tile into every peer's output")):
-            fused = colsplit.PeerColumnSplit(M, N, K, device=dev, mode=mode)
+        for mode, layout, what in (
+                ("dma", "blocks", "[G,M,N/G] blocks like NCCL's; 4096-row chunks, each pushed to every peer as one "
+                                  "contiguous copy by the copy engines while the next chunk computes"),
+                ("dma", "rows", "[M,N]; 4096-row chunks pushed as 2-D copies while the next chunk computes"),
+                ("stores", "rows", "[M,N]; the GEMM epilogue stores each tile into every peer's output")):
+            fused = colsplit.PeerColumnSplit(M, N, K, device=dev, mode=mode, layout=layout)
             for _ in range(3):
                 fused(xs, q_s, s_s, b_s)
             torch.cuda.synchronize(dev)
@@ -494,9 +496,9 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
             ends[0].record(stream)
             torch.cuda.synchronize(dev)
             ms = reduce_max(e0.elapsed_time(ends[0]) / steps)
-            out[f"colsplit_linear_peer_{mode}"] = {
+            out[f"colsplit_linear_peer_{mode}_{layout}"] = {
                 "workload": f"config-1 linear, W rows split {world} ways, x replicated, written into all {world} "
-                            f"GPUs' [{M},{N}] outputs over NVLink (CUDA IPC mappings): {what}",
+                            f"GPUs' outputs over NVLink (CUDA IPC mappings), M={M} N={N}: {what}",
                 "ms_per_step": round(ms, 4), "value": round(OPS_PER_STEP / (ms * 1e-3) / 1e12, 1), "unit": "TOPS",
                 "scaling": "strong", "nvlink_bytes_out_per_gpu": (world - 1) * M * nl * 2, "steps": steps}
             fused.close()

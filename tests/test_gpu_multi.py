@@ -52,17 +52,19 @@ def _worker(rank, world, port, result_dir):
             assert torch.equal(blocks[g], full[:, g * n // world:(g + 1) * n // world])
         # the all-gather inside the GEMM epilogue (peer stores over NVLink)
         for mode in ("dma", "stores"):
-            fused = colsplit.PeerColumnSplit(m, n, k, device=dev, mode=mode, chunk_rows=384)
-            try:
-                for _ in range(2):  # twice: the buffer is reused
-                    y = fused(x, q_s, s_s, b_s)
-                    torch.cuda.synchronize(dev)
-                    assert torch.equal(y, full), mode
-                y = fused(x[:37], q_s, s_s, b_s)
-                torch.cuda.synchronize(dev)
-                assert torch.equal(y, full[:37]), mode
-            finally:
-                fused.close()
+            for layout in ("rows", "blocks"):
+                fused = colsplit.PeerColumnSplit(m, n, k, device=dev, mode=mode, chunk_rows=384, layout=layout)
+                try:
+                    for mm in (m, m, 37):  # the buffer is reused; then a short batch
+                        y = fused(x[:mm], q_s, s_s, b_s)
+                        torch.cuda.synchronize(dev)
+                        if layout == "rows":
+                            assert torch.equal(y, full[:mm]), (mode, layout)
+                        else:
+                            for g in range(world):
+                                assert torch.equal(y[g], full[:mm, g * n // world:(g + 1) * n // world]), (mode, layout)
+                finally:
+                    fused.close()
         assert _native.device_error() == 0
         Path(result_dir, f"ok{rank}").write_text("ok")
     finally:

@@ -81,9 +81,13 @@ class PeerColumnSplit:
 
       mode="dma"     the token rows are processed in chunks; each chunk's GEMM writes this
                      rank's column block into the local output, and the copy engines push the
-                     finished chunk to every peer (2-D peer copies, one stream per peer) while
-                     the next chunk computes;
+                     finished chunk to every peer (one stream per peer) while the next chunk
+                     computes;
       mode="stores"  the GEMM epilogue itself stores every tile into all ranks' outputs.
+
+    layout="rows" gives the [M, N] output (a pushed chunk is a 2-D copy of rows of N/G
+    columns); layout="blocks" gives [G, M, N/G] as NCCL's all-gather does (block g holds
+    columns [g*N/G, (g+1)*N/G); a pushed chunk is one contiguous copy).
 
     One instance per process (rank), created collectively; it owns the [m_max, n_full] bf16
     output buffer this rank exposes to its peers (allocated by the library with a CUDA IPC
@@ -94,7 +98,7 @@ class PeerColumnSplit:
     """
 
     def __init__(self, m_max: int, n_full: int, k: int, device=None, group=None, mode: str = "dma",
-                 chunk_rows: int = 4096):
+                 chunk_rows: int = 4096, layout: str = "rows"):
         import ctypes
 
         from . import _native as nat
@@ -109,7 +113,11 @@ class PeerColumnSplit:
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         if mode not in ("dma", "stores"):
             raise ValueError("mode must be 'dma' or 'stores'")
-        self.mode, self.chunk_rows = mode, max(1, chunk_rows)
+        if layout not in ("rows", "blocks"):
+            raise ValueError("layout must be 'rows' or 'blocks'")
+        if n_full % (8 * self.world):
+            raise ValueError(f"n_full {n_full} must split into {self.world} shards that are multiples of 8")
+        self.mode, self.chunk_rows, self.layout = mode, max(1, chunk_rows), layout
         self.m_max, self.n_full, self.k = m_max, n_full, k
         self._copy_streams = [torch.cuda.Stream(device=self.device) for _ in range(max(0, self.world - 1))]
         self.lib = nat.load()
@@ -170,38 +178,47 @@ class PeerColumnSplit:
         x = x.contiguous()
         sw = ops._vec(wscales_shard, nl, torch.float32, self.device, "wscales_shard")
         b = ops._vec(bias_shard, nl, torch.bfloat16, self.device, "bias_shard")
-        col0 = self.rank * nl * 2  # bytes
+        if self.layout == "rows":
+            base, ldo = self.rank * nl * 2, self.n_full  # this rank's columns inside [M, N]
+        else:
+            base, ldo = self.rank * self.m_max * nl * 2, nl  # this rank's block of [G, M, N/G]
+        pitch = ldo * 2
         peers = [r for r in range(self.world) if r != self.rank]
         cur = torch.cuda.current_stream(self.device)
         dist.all_reduce(self._flag, group=self.group)  # every rank is done with the previous result
         with torch.cuda.device(self.device):
             if self.mode == "stores":
-                outs = [self.ptrs[self.rank] + col0] + [self.ptrs[r] + col0 for r in peers]
-                self._linear(x, qweight_shard, sw, b, outs, 0, m, nl, epilogue, cur)
+                outs = [self.ptrs[self.rank] + base] + [self.ptrs[r] + base for r in peers]
+                self._linear(x, qweight_shard, sw, b, outs, ldo, 0, m, nl, epilogue, cur)
             else:
-                pitch = self.n_full * 2
-                events = []
                 for r0 in range(0, m, self.chunk_rows):
                     rows = min(self.chunk_rows, m - r0)
-                    self._linear(x, qweight_shard, sw, b, [self.ptrs[self.rank] + col0], r0, rows, nl, epilogue, cur)
+                    self._linear(x, qweight_shard, sw, b, [self.ptrs[self.rank] + base], ldo, r0, rows, nl, epilogue,
+                                 cur)
                     ev = torch.cuda.Event()
                     ev.record(cur)
-                    events.append(ev)
-                    off = r0 * pitch + col0
+                    off = base + r0 * pitch
                     for s, r in zip(self._copy_streams, peers):
                         s.wait_event(ev)
-                        nat.check(self.lib.slim_copy_2d(self.ptrs[r] + off, pitch, self.ptrs[self.rank] + off, pitch,
-                                                        nl * 2, rows, s.cuda_stream))
+                        if self.layout == "rows":
+                            nat.check(self.lib.slim_copy_2d(self.ptrs[r] + off, pitch, self.ptrs[self.rank] + off,
+                                                            pitch, nl * 2, rows, s.cuda_stream))
+                        else:  # the chunk's rows of this rank's block are contiguous
+                            nbytes = rows * pitch
+                            nat.check(self.lib.slim_copy_2d(self.ptrs[r] + off, nbytes, self.ptrs[self.rank] + off,
+                                                            nbytes, nbytes, 1, s.cuda_stream))
                 for s in self._copy_streams:
                     cur.wait_stream(s)
         dist.all_reduce(self._flag, group=self.group)  # every rank's data has landed
-        return self.buf[:m]
+        if self.layout == "rows":
+            return self.buf[:m]
+        return self.buf.view(-1)[: self.world * self.m_max * nl].view(self.world, self.m_max, nl)[:, :m]
 
-    def _linear(self, x, qw, sw, b, outs, r0, rows, nl, epilogue, stream):
+    def _linear(self, x, qw, sw, b, outs, ldo, r0, rows, nl, epilogue, stream):
         from . import ops
 
-        arr = (self._ct.c_void_p * len(outs))(*[o + r0 * self.n_full * 2 for o in outs])
+        arr = (self._ct.c_void_p * len(outs))(*[o + r0 * ldo * 2 for o in outs])
         self._nat.check(self.lib.slim_int8_linear_colsplit(
             x.data_ptr() + r0 * self.k * x.element_size(), ops._DT[x.dtype], qw.data_ptr(), sw.data_ptr(), ops._ptr(b),
-            arr, len(outs), self.n_full, self.xq.data_ptr() + r0 * self.k, self.sx.data_ptr() + r0 * 4, rows, nl,
+            arr, len(outs), ldo, self.xq.data_ptr() + r0 * self.k, self.sx.data_ptr() + r0 * 4, rows, nl,
             self.k, 256, ops._EPI[epilogue], stream.cuda_stream))
