@@ -228,6 +228,46 @@ int slim_rel_l2_int8(const int8_t* qa, const float* sa, const int8_t* qb, const 
 int slim_rel_l2(const void* a, int a_dtype, const void* b, int b_dtype, int64_t n,
                 double* out2, void* stream);
 
+/* ---------------------------------------------------------------- attention
+ * In-place INT8/FP8 flash attention on the DiT's packed qkv buffer: the reference's
+ * TritonAttnOverride._run (comfyui/ComfyUI-SlimDiT/attention_triton.py:265-299) and its
+ * kernels quant_int8_rows, tensor_amax, quant_fp8_global and flash_int8 (:79-174).
+ * Head dim 128 only. seq_pad is seq rounded up to a multiple of 128 (or larger, a multiple of
+ * 128); per-head scale rows are [heads, seq_pad] fp32 and their padding is written as 0. */
+
+/* Bytes of the workspace slim_attn_packed needs for (seq, heads, dim). */
+int slim_attn_workspace_bytes(int64_t seq, int heads, int dim, uint64_t* bytes);
+
+/* q and k rows of the bf16 buffer qkv (row pitch row_stride elements; q at column q_offset,
+ * k at k_offset): rotate != 0 applies the +-1 Sylvester Hadamard over each (token, head)
+ * row first; scale = max(amax, 1e-8) / 127, code = clip(floor(x / scale + 0.5), -127, 127)
+ * (quant_int8_rows, attention_triton.py:79-102). q, k: int8 [seq, heads*dim];
+ * q_scale_t, k_scale_t: fp32 [heads, seq_pad]. */
+int slim_attn_quant_qk(const void* qkv, int64_t seq, int heads, int dim, int64_t row_stride,
+                       int64_t q_offset, int64_t k_offset, int rotate, int8_t* q,
+                       float* q_scale_t, int8_t* k, float* k_scale_t, int64_t seq_pad,
+                       void* stream);
+
+/* v rows of qkv (column v_offset) -> *v_amax = max|v| (device fp32 scalar) and
+ * v_t = E4M3(v / max(amax / 448, 1e-8)), transposed per head: uint8 [heads, dim, seq_pad],
+ * zero padded (tensor_amax + quant_fp8_global, attention_triton.py:104-129, 283-287). */
+int slim_attn_quant_v(const void* qkv, int64_t seq, int heads, int dim, int64_t row_stride,
+                      int64_t v_offset, uint8_t* v_t, int64_t seq_pad, float* v_amax,
+                      void* stream);
+
+/* out[seq, ldo] bf16 (head h at columns [h*dim, h*dim+dim)) = softmax attention of the
+ * quantised q/k/v above with logits s * q_scale * k_scale * attn_scale, P rounded to E4M3
+ * for both P V and the row sum (flash_int8, attention_triton.py:131-174). */
+int slim_attn_int8(const int8_t* q, const float* q_scale_t, const int8_t* k,
+                   const float* k_scale_t, const uint8_t* v_t, const float* v_amax,
+                   float attn_scale, int64_t seq, int heads, int dim, int64_t seq_pad,
+                   void* out, int64_t ldo, void* stream);
+
+/* The whole override on a packed [seq, 3*heads*dim] bf16 buffer: the three calls above with
+ * attn_scale = dim^-0.5 / (rotate ? dim : 1); out bf16 [seq, heads*dim]. */
+int slim_attn_packed(const void* qkv, int64_t seq, int heads, int dim, int rotate, void* out,
+                     void* workspace, uint64_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

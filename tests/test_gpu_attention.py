@@ -1,0 +1,214 @@
+"""GPU parity of the in-place INT8/FP8 flash attention (slimdit.attention, csrc/attn.cu)
+against the oracle's restatement of the reference's attention_triton.py.
+
+* the quantisers are bit-exact: q/k codes and per-(token, head) scales (rotated and not), the
+  V amax and the transposed E4M3 codes;
+* the flash kernel, fed the same codes, matches the oracle's online softmax within the
+  tolerance of the hardware exponential (ATOL_FRAC below);
+* the whole override tracks unquantised fp64 attention as closely as the oracle's restatement
+  does (cosine within 1e-4 of the oracle's, and above 0.99 on this heavy-tailed data; the
+  reference quotes 0.99932 on its own activations at S=30026, attention_triton.py:25);
+* the ComfyUI override dispatches packed views to the kernel and everything else to the
+  model's own attention.
+"""
+
+import sys
+import types
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import oracle.attention as oa
+
+pytestmark = pytest.mark.gpu
+
+D = 128
+# Output tolerance against the oracle. The GPU's ex2.approx is within a few fp32 ulps of the
+# oracle's exact exp2, so a P value next to an E4M3 rounding midpoint can round one FP8 step
+# the other way (one in ~10^5 values). Outputs are bf16: most elements agree exactly, a few
+# differ by one bf16 ulp (fp32 accumulation order in the tensor core), and a flipped P moves
+# an output by at most 2^-4 * p * (|v| + |out|) / l.
+ULP_FRAC = 0.02           # fraction of outputs allowed beyond 1 bf16 ulp
+REL_L2 = 2e-3             # relative L2 distance of the whole output
+ATOL_FRAC = 0.13          # max abs difference, as a fraction of max |v|
+
+
+def packed_qkv(seq, heads, seed, scale=0.5, outliers=True):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_t(4, size=(seq, 3 * heads * D)).astype(np.float32) * np.float32(scale)
+    if outliers:
+        cols = rng.choice(3 * heads * D, size=6, replace=False)
+        x[:, cols] *= 12.0
+    return oracle.bf16_round(x)
+
+
+def to_dev(x):
+    return torch.from_numpy(x).to("cuda").to(torch.bfloat16)
+
+
+def check_close(gpu, ref, vmax, what):
+    gpu = np.asarray(gpu, np.float64)
+    ref = np.asarray(ref, np.float64)
+    assert np.all(np.isfinite(gpu)), f"{what}: non-finite output"
+    diff = np.abs(gpu - ref)
+    beyond = diff > oracle.bf16_ulp(ref) * 1.001
+    rel = np.linalg.norm(gpu - ref) / max(np.linalg.norm(ref), 1e-30)
+    assert beyond.mean() <= ULP_FRAC, f"{what}: {beyond.mean():.4%} of outputs beyond 1 bf16 ulp"
+    assert rel <= REL_L2, f"{what}: relative L2 {rel:.3e}"
+    assert diff.max() <= ATOL_FRAC * vmax, f"{what}: max abs diff {diff.max():.3e} (max |v| {vmax:.3e})"
+
+
+@pytest.mark.parametrize("rotate", [True, False])
+@pytest.mark.parametrize("seq,heads", [(300, 3), (128, 1), (1, 2)])
+def test_quantisers_bit_exact(cuda, seq, heads, rotate):
+    from slimdit import _native, attention
+
+    x = packed_qkv(seq, heads, seed=seq + heads)
+    ops = attention.quantized_operands(to_dev(x), heads, rotate=rotate)
+    torch.cuda.synchronize()
+    q, k, v = oa.split_packed(x, heads, D)
+    q8, qs = oa.quant_qk(q, rotate)
+    k8, ks = oa.quant_qk(k, rotate)
+    v8, amax = oa.quant_v(v)
+    pad = ops["seq_pad"]
+    assert pad == (seq + 127) // 128 * 128
+    assert np.array_equal(ops["q"].cpu().numpy(), q8.reshape(seq, -1))
+    assert np.array_equal(ops["k"].cpu().numpy(), k8.reshape(seq, -1))
+    for got, want in ((ops["q_scale"], qs), (ops["k_scale"], ks)):
+        g = got.cpu().numpy()
+        assert np.array_equal(g[:, :seq].view(np.uint32), want.T.copy().view(np.uint32))
+        assert not g[:, seq:].any(), "scale padding must be zero"
+    assert ops["v_amax"].item() == float(amax)
+    assert np.array_equal(ops["v"].cpu().numpy(), oa.transpose_v(v8, pad))
+    assert _native.device_error() == 0
+
+
+@pytest.mark.parametrize("seq,heads", [(1000, 2), (256, 1), (77, 1)])
+def test_flash_matches_oracle(cuda, seq, heads):
+    from slimdit import _native, attention
+
+    x = packed_qkv(seq, heads, seed=7 * seq + heads)
+    ops = attention.quantized_operands(to_dev(x), heads, rotate=True)
+    scale = attention.attn_scale(D, True)
+    out = attention.attention_quantized(ops, seq, heads, scale)
+    torch.cuda.synchronize()
+    q, k, v = oa.split_packed(x, heads, D)
+    q8, qs = oa.quant_qk(q, True)
+    k8, ks = oa.quant_qk(k, True)
+    v8, amax = oa.quant_v(v)
+    ref = oa.flash(q8, qs, k8, ks, v8, amax, np.float32(scale)).reshape(seq, -1)
+    check_close(out.float().cpu().numpy(), ref, float(amax), f"flash seq={seq}")
+    assert _native.device_error() == 0
+
+
+def test_packed_override_tracks_dense_attention(cuda):
+    from slimdit import _native, attention
+
+    seq, heads = 2100, 2
+    x = packed_qkv(seq, heads, seed=11)
+    out = attention.attention_packed(to_dev(x), heads, rotate=True)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy().astype(np.float64)
+    ref = oa.attention_packed(x, heads, D, rotate=True)
+    q, k, v = oa.split_packed(x, heads, D)
+    check_close(got, ref, float(np.abs(v).max()), "packed")
+    dense = oa.dense_attention_f64(x, heads, D)
+
+    def cosine(a):
+        return float((a * dense).sum() / np.linalg.norm(a) / np.linalg.norm(dense))
+
+    assert abs(cosine(got) - cosine(ref)) <= 1e-4, (cosine(got), cosine(ref))
+    assert cosine(got) >= 0.99
+    assert _native.device_error() == 0
+
+
+def test_unrotated_and_strided_rows(cuda):
+    """rotate=False, and a packed buffer whose rows are longer than 3*H*D (general pitch path)."""
+    from slimdit import attention
+
+    seq, heads = 513, 1
+    x = packed_qkv(seq, heads, seed=5)
+    wide = np.zeros((seq, 3 * heads * D + 64), np.float32)
+    wide[:, :3 * heads * D] = x
+    buf = to_dev(wide)
+    out = attention.attention_packed(buf[:, :3 * heads * D], heads, rotate=False)
+    torch.cuda.synchronize()
+    ref = oa.attention_packed(x, heads, D, rotate=False)
+    check_close(out.float().cpu().numpy(), ref, float(np.abs(x[:, 2 * heads * D:]).max()), "unrotated")
+
+
+def test_long_sequence_one_head(cuda):
+    from slimdit import attention
+
+    seq, heads = 4096 + 77, 1
+    x = packed_qkv(seq, heads, seed=3, scale=1.0)
+    out = attention.attention_packed(to_dev(x), heads)
+    torch.cuda.synchronize()
+    ref = oa.attention_packed(x, heads, D)
+    check_close(out.float().cpu().numpy(), ref, float(np.abs(x[:, 2 * D:]).max()), "long")
+
+
+def test_bad_shapes_and_alignment(cuda):
+    from slimdit import _native, attention
+
+    lib = _native.load()
+    st = torch.cuda.current_stream().cuda_stream
+    buf = torch.zeros((256, 3 * 64), dtype=torch.bfloat16, device="cuda")
+    ws = torch.empty((1 << 20,), dtype=torch.uint8, device="cuda")
+    out = torch.empty((256, 64), dtype=torch.bfloat16, device="cuda")
+    assert lib.slim_attn_packed(buf.data_ptr(), 256, 1, 64, 1, out.data_ptr(), ws.data_ptr(), ws.numel(), st) \
+        == _native.SLIM_ERR_SHAPE
+    x = to_dev(packed_qkv(256, 1, seed=1))
+    assert lib.slim_attn_packed(x.data_ptr(), 256, 1, 128, 1, out.data_ptr(), ws.data_ptr(), 16, st) \
+        == _native.SLIM_ERR_SHAPE  # workspace too small
+    assert lib.slim_attn_packed(x.data_ptr() + 2, 255, 1, 128, 1, out.data_ptr(), ws.data_ptr(), ws.numel(), st) \
+        == _native.SLIM_ERR_ALIGN
+    with pytest.raises(ValueError):
+        attention.attention_packed(x[:, :3 * 64], 1)
+    assert _native.device_error() == 0
+
+
+def _fake_comfy(monkeypatch):
+    calls = []
+
+    def original(q, k, v, heads, mask=None, skip_reshape=False, skip_output_reshape=False, **kw):
+        calls.append(mask)
+        return "dense"
+
+    mod = types.ModuleType("comfy.ldm.minimax.model")
+    mod.optimized_attention = original
+    for name in ("comfy", "comfy.ldm", "comfy.ldm.minimax"):
+        monkeypatch.setitem(sys.modules, name, types.ModuleType(name))
+    monkeypatch.setitem(sys.modules, "comfy.ldm.minimax.model", mod)
+    return mod, calls
+
+
+def test_comfy_override_dispatch(cuda, monkeypatch):
+    from slimdit import attention
+
+    mod, calls = _fake_comfy(monkeypatch)
+    stats = {}
+    ov = attention.install_triton_attn(attention.TritonAttnConfig(enabled=True, min_seq=256), stats=stats)
+    assert mod.optimized_attention is ov
+    seq, heads = 300, 2
+    x = packed_qkv(seq, heads, seed=9)
+    buf = to_dev(x)
+    view = buf.view(1, seq, 3, heads, D)
+    q, k, v = (view[:, :, i].permute(0, 2, 1, 3) for i in range(3))  # (1, heads, seq, dim) views
+    y = mod.optimized_attention(q, k, v, heads, skip_reshape=True)
+    assert y.shape == (1, seq, heads * D)
+    ref = attention.attention_packed(buf, heads)
+    assert torch.equal(y[0], ref)
+    y2 = mod.optimized_attention(q, k, v, heads, skip_reshape=True, skip_output_reshape=True)
+    assert y2.shape == (1, heads, seq, D) and torch.equal(y2.transpose(1, 2).reshape(seq, -1), ref)
+    # a mask, a copy instead of the packed view, or a short sequence go to the model's attention
+    assert mod.optimized_attention(q, k, v, heads, mask=torch.ones(1), skip_reshape=True) == "dense"
+    assert mod.optimized_attention(q.contiguous(), k, v, heads, skip_reshape=True) == "dense"
+    short = buf[:100].view(1, 100, 3, heads, D)
+    qs, ks, vs = (short[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+    assert mod.optimized_attention(qs, ks, vs, heads, skip_reshape=True) == "dense"
+    assert stats["kernel_calls"] == 2 and stats["fallback_calls"] == 3
+    ov.uninstall()
+    assert mod.optimized_attention is not ov

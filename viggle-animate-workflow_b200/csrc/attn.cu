@@ -1,0 +1,841 @@
+// In-place INT8/FP8 flash attention for the packed qkv buffer of the Viggle / MiniMax-H3 DiT
+// (the reference's comfyui/ComfyUI-SlimDiT/attention_triton.py), on sm_100a tensor cores.
+//
+// The DiT hands attention three strided views of one packed [S, 3*H*D] bf16 buffer (q at
+// column 0, k at H*D, v at 2*H*D; attention_triton.py:185-212). The override quantises in
+// place instead of copying:
+//
+//   quant_qk_kernel   q and k rows of D=128 per (token, head), optionally rotated by the
+//                     unnormalised +-1 Sylvester Hadamard (attention_triton.py:47-63, 79-102):
+//                     fp64 fast Walsh-Hadamard transform (exact for every input whose
+//                     magnitudes in one row span less than 2^45) rounded once to fp32, then
+//                     scale = max(amax, 1e-8) / 127, q = clip(floor(x / scale + 0.5), +-127).
+//                     Codes go to [S, H*D] (the reference layout); scales to [H, S_pad]
+//                     (contiguous per head, so the attention kernel bulk-loads a key tile's).
+//   v_amax_kernel     max |v| over the whole tensor (attention_triton.py:104-115, 283-286).
+//   quant_v_kernel    v / max(amax / 448, 1e-8) rounded to E4M3 (nearest even, saturating;
+//                     :117-129), written transposed per head as [H, D, S_pad] so that the PV
+//                     product reads V as a K-major operand.
+//   flash_kernel      one CTA per (128-query tile, head), 10 warps (flash_int8, :131-174):
+//     warp 0       TMA producer: Q tile once; per key tile the K tile (128 keys x 128 B), the
+//                  V^T tile (128 value columns x 128 keys) and 128 key scales (bulk copy) into
+//                  a 3-stage ring.
+//     warp 1       TMEM (512 columns: S int32 [0,128), O buffers at 128 and 288) and one lane
+//                  issuing the MMAs: S = Q K^T (kind::i8, M=N=128) and O_j = P_j V_j
+//                  (kind::f8f6f4 E4M3, M=128, N=144). V's smem tile carries 16 extra rows,
+//                  the first all ones: column 128 of O_j is the row sum of the FP8-rounded
+//                  P_j, i.e. the reference's l increment, from the same tensor-core pass.
+//     warps 2..5   softmax, one query row per thread: S row from TMEM, y = float(s) * ks,
+//                  running max, alpha = 2^(m - m'), p = 2^(y*ra - m') with the hardware ex2,
+//                  E4M3 pairs written into a 128-byte-swizzled P tile (the PV A operand).
+//     warps 6..9   correction, one row per thread: acc = acc * alpha + O_j, l likewise,
+//                  from double-buffered O tiles; finally out = bf16(acc * v_scale / l).
+//   The MMA lane issues S_{j+1} before P_j V_j, so the softmax of tile j+1 never waits for
+//   the PV product of tile j. Every mbarrier wait is bounded (slim_ptx.cuh).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "../../include/slimdit_b200.h"
+#include "slim_kernels.h"
+#include "slim_ptx.cuh"
+
+namespace slim {
+namespace attn {
+
+constexpr int D = 128;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ---------------------------------------------------------------- Q / K quantiser
+// Four lanes per (token, head) row: lane sub = lane & 3 holds elements [32 sub, 32 sub + 32).
+__device__ __forceinline__ void load32_bf16(const __nv_bfloat16* src, float (&x)[32]) {
+  const uint4* p = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    const uint4 u = __ldg(p + v);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      x[8 * v + 2 * e] = __uint_as_float(w[e] << 16);
+      x[8 * v + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) quant_qk_kernel(const __nv_bfloat16* __restrict__ src, int64_t seq,
+                                                       int64_t seq_pad, int heads, int64_t row_stride,
+                                                       int64_t q_off, int64_t k_off, int rotate,
+                                                       int8_t* __restrict__ q_out, float* __restrict__ qs_t,
+                                                       int8_t* __restrict__ k_out, float* __restrict__ ks_t) {
+  const int lane = threadIdx.x & 31;
+  const int sub = lane & 3;
+  const int64_t per_tensor = seq_pad * heads;
+  const int64_t tasks = 2 * per_tensor;
+  const int64_t groups = (tasks + 7) / 8;  // eight rows per warp
+  const int64_t first = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t step = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  // the loop is uniform per warp: every lane takes part in the shuffles
+  for (int64_t g = first; g < groups; g += step) {
+    const int64_t t = g * 8 + (lane >> 2);
+    const bool in = t < tasks;
+    const bool is_k = t >= per_tensor;
+    const int64_t r = is_k ? t - per_tensor : t;
+    const int64_t token = in ? r / heads : 0;
+    const int head = in ? static_cast<int>(r - token * heads) : 0;
+    float* scale_t = is_k ? ks_t : qs_t;
+    const bool live = in && token < seq;
+    if (in && !live && sub == 0) scale_t[head * seq_pad + token] = 0.0f;  // padding of the scale rows
+    float x[32];
+    if (live) {
+      load32_bf16(src + token * row_stride + (is_k ? k_off : q_off) + head * D + sub * 32, x);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) x[e] = 0.0f;
+    }
+    float y[32];
+    if (rotate) {
+      double v[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] = static_cast<double>(x[e]);
+#pragma unroll
+      for (int h = 1; h < 32; h <<= 1) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          if (e & h) continue;
+          const double a = v[e], b = v[e + h];
+          v[e] = a + b;
+          v[e + h] = a - b;
+        }
+      }
+#pragma unroll
+      for (int bit = 1; bit <= 2; bit <<= 1) {  // strides 32 and 64: across the four lanes
+        const bool upper = (sub & bit) != 0;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const double o = __shfl_xor_sync(0xffffffffu, v[e], bit);
+          v[e] = upper ? o - v[e] : v[e] + o;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 32; ++e) y[e] = __double2float_rn(v[e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) y[e] = x[e];
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(y[e]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
+    uint32_t packed[8];
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        float c = floorf(__fadd_rn(__fdiv_rn(y[4 * w + b], scale), 0.5f));
+        c = fminf(fmaxf(c, -127.0f), 127.0f);
+        word |= (static_cast<uint32_t>(static_cast<int>(c)) & 0xffu) << (8 * b);
+      }
+      packed[w] = word;
+    }
+    if (!live) continue;
+    int8_t* dst = (is_k ? k_out : q_out) + token * (static_cast<int64_t>(heads) * D) + head * D + sub * 32;
+    reinterpret_cast<uint4*>(dst)[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    reinterpret_cast<uint4*>(dst)[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+    if (sub == 0) scale_t[head * seq_pad + token] = scale;
+  }
+}
+
+// ---------------------------------------------------------------- V: amax, E4M3, transpose
+__global__ void __launch_bounds__(256) v_amax_kernel(const __nv_bfloat16* __restrict__ src, int64_t seq, int heads,
+                                                     int64_t row_stride, int64_t v_off, float* __restrict__ amax) {
+  const int64_t vecs = static_cast<int64_t>(heads) * D / 8;  // 16-byte vectors per token
+  const int64_t total = seq * vecs;
+  float m = 0.0f;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t token = i / vecs;
+    const int64_t v = i - token * vecs;
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(src + token * row_stride + v_off) + v);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[e] << 16)), fabsf(__uint_as_float(w[e] & 0xffff0000u))));
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<unsigned int*>(amax), __float_as_uint(m));
+}
+
+__device__ __forceinline__ float v_scale_of(float amax) { return fmaxf(__fdiv_rn(amax, 448.0f), 1e-8f); }
+
+// One block per (128-token tile, head): 256 threads, thread t converts token t/2, value
+// columns [64 (t%2), +64), and the tile leaves through shared memory transposed.
+constexpr int VT_PITCH = 144;  // bytes per transposed row in shared memory (128 tokens + pad)
+
+__global__ void __launch_bounds__(256) quant_v_kernel(const __nv_bfloat16* __restrict__ src, int64_t seq,
+                                                      int64_t seq_pad, int heads, int64_t row_stride, int64_t v_off,
+                                                      const float* __restrict__ amax, uint8_t* __restrict__ v_t) {
+  __shared__ __align__(16) uint8_t tile[D * VT_PITCH];
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * 128;
+  const int head = blockIdx.y;
+  const float vs = v_scale_of(__ldg(amax));
+  const int tok = threadIdx.x >> 1;
+  const int half = threadIdx.x & 1;
+  const int64_t token = t0 + tok;
+  const uint4* p = reinterpret_cast<const uint4*>(src + token * row_stride + v_off + head * D + half * 64);
+#pragma unroll
+  for (int v = 0; v < 8; ++v) {
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (token < seq) u = __ldg(p + v);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float a = __fdiv_rn(__uint_as_float(w[e] << 16), vs);
+      const float b = __fdiv_rn(__uint_as_float(w[e] & 0xffff0000u), vs);
+      const __nv_fp8x2_storage_t pr = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+      const int d = half * 64 + v * 8 + 2 * e;
+      tile[d * VT_PITCH + tok] = static_cast<uint8_t>(pr & 0xff);
+      tile[(d + 1) * VT_PITCH + tok] = static_cast<uint8_t>(pr >> 8);
+    }
+  }
+  __syncthreads();
+  const int d = threadIdx.x >> 1;
+  const uint4* s = reinterpret_cast<const uint4*>(tile + d * VT_PITCH + half * 64);
+  uint4* g = reinterpret_cast<uint4*>(v_t + (static_cast<int64_t>(head) * D + d) * seq_pad + t0 + half * 64);
+#pragma unroll
+  for (int v = 0; v < 4; ++v) g[v] = s[v];
+}
+
+// ---------------------------------------------------------------- flash kernel
+namespace fl {
+constexpr int BM = 128;           // query rows per CTA
+constexpr int BN = 128;           // keys per tile
+constexpr int NV = 144;           // PV MMA N: 128 value columns + 16 rows (the first all ones)
+constexpr int ST = 3;             // K/V ring depth
+constexpr int AR = 4;             // alpha ring depth
+constexpr int Q_BYTES = BM * D;
+constexpr int K_BYTES = BN * D;
+constexpr int VT_BYTES = D * BN;  // the TMA part of a V stage
+constexpr int V_BYTES = NV * BN;
+constexpr int KS_BYTES = BN * 4;
+constexpr int P_BYTES = BM * BN;
+constexpr int THREADS = 320;
+constexpr int TMEM_COLS = 512;
+constexpr uint32_t COL_S = 0;
+constexpr uint32_t COL_O0 = 128, COL_O1 = 288;  // the two O tiles (144 columns each)
+__device__ __forceinline__ uint32_t col_o(int b) { return b ? COL_O1 : COL_O0; }
+constexpr int MMA_K = 32;
+constexpr uint32_t IDESC_QK = idesc_i8(BM, BN);
+constexpr uint32_t IDESC_PV = idesc_f8_e4m3(BM, NV);
+
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + Q_BYTES;
+constexpr int OFF_V = OFF_K + ST * K_BYTES;
+constexpr int OFF_P = OFF_V + ST * V_BYTES;
+constexpr int OFF_KS = OFF_P + 2 * P_BYTES;
+constexpr int OFF_SH = OFF_KS + ST * KS_BYTES;
+
+struct Shared {
+  uint64_t q_full;
+  uint64_t kv_full[ST];
+  uint64_t kv_empty[ST];
+  uint64_t s_full;
+  uint64_t s_free;
+  uint64_t p_full[2];
+  uint64_t p_free[2];
+  uint64_t o_full[2];
+  uint64_t o_free[2];
+  uint64_t a_full[AR];
+  uint64_t a_free[AR];
+  uint64_t drain;
+  uint32_t tmem_base;
+  volatile int abort;
+  float alpha[AR][BM];
+};
+constexpr size_t SMEM_BYTES = 1024 + OFF_SH + sizeof(Shared);
+
+static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && OFF_P % 1024 == 0 && V_BYTES % 1024 == 0,
+              "operand tiles must stay 1024-byte aligned for the 128-byte swizzle");
+
+struct Params {
+  const float* qs_t;   // [H, seq_pad]
+  const float* ks_t;   // [H, seq_pad]
+  const float* v_amax; // device scalar
+  __nv_bfloat16* out;  // [seq, ldo]
+  int64_t ldo;
+  int64_t seq, seq_pad;
+  float attn_scale;
+};
+
+__global__ void __launch_bounds__(384, 1)
+flash_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+             const __grid_constant__ CUtensorMap tv, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
+  uint8_t* sQ = smem + OFF_Q;
+  uint8_t* sK = smem + OFF_K;
+  uint8_t* sV = smem + OFF_V;
+  uint8_t* sP = smem + OFF_P;
+  uint8_t* sKS = smem + OFF_KS;
+  Shared& sh = *reinterpret_cast<Shared*>(smem + OFF_SH);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int head = blockIdx.y;
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * BM;
+  const int nk = static_cast<int>((p.seq + BN - 1) / BN);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sh.q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&sh.kv_full[s], 1);
+      mbar_init(&sh.kv_empty[s], 1);
+    }
+    mbar_init(&sh.s_full, 1);
+    mbar_init(&sh.s_free, 4);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sh.p_full[b], 128);
+      mbar_init(&sh.p_free[b], 1);
+      mbar_init(&sh.o_full[b], 1);
+      mbar_init(&sh.o_free[b], 128);
+    }
+    for (int a = 0; a < AR; ++a) {
+      mbar_init(&sh.a_full[a], 128);
+      mbar_init(&sh.a_free[a], 128);
+    }
+    mbar_init(&sh.drain, 1);
+    sh.abort = 0;
+    fence_mbar_init();
+  }
+  // Rows 128..143 of every V stage: row 128 = E4M3 1.0 (0x38) for all keys, the rest 0.
+  for (int i = threadIdx.x; i < ST * (V_BYTES - VT_BYTES) / 16; i += blockDim.x) {
+    const int s = i / ((V_BYTES - VT_BYTES) / 16);
+    const int w = i % ((V_BYTES - VT_BYTES) / 16);
+    const uint32_t f = w < BN / 16 ? 0x38383838u : 0u;
+    *reinterpret_cast<uint4*>(sV + s * V_BYTES + VT_BYTES + w * 16) = make_uint4(f, f, f, f);
+  }
+  fence_proxy_async_smem();
+  if (warp == 1) {
+    tmem_alloc(&sh.tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      mbar_arrive_expect_tx(&sh.q_full, Q_BYTES);
+      tma_load_2d(sQ, &tq, &sh.q_full, head * D, static_cast<int32_t>(q0));
+      uint32_t issued = 0, last_parity = 0;
+      const float* ks_head = p.ks_t + head * p.seq_pad;
+      for (int j = 0; j < nk && !sh.abort; ++j) {
+        const int s = j % ST;
+        const uint32_t ph = (j / ST) & 1;
+        if (!mbar_wait(&sh.kv_empty[s], ph ^ 1, kErrWaitTimeoutProducer)) {
+          sh.abort = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&sh.kv_full[s], K_BYTES + VT_BYTES + KS_BYTES);
+        tma_load_2d(sK + s * K_BYTES, &tk, &sh.kv_full[s], head * D, j * BN);
+        tma_load_2d(sV + s * V_BYTES, &tv, &sh.kv_full[s], j * BN, head * D);
+        bulk_load(sKS + s * KS_BYTES, ks_head + static_cast<int64_t>(j) * BN, KS_BYTES, &sh.kv_full[s]);
+        issued |= 1u << s;
+        last_parity = (last_parity & ~(1u << s)) | (ph << s);
+      }
+      // every load issued by this thread lands before the CTA may exit
+      mbar_wait(&sh.q_full, 0, kErrWaitTimeoutDrain);
+      for (int s = 0; s < ST; ++s)
+        if (issued & (1u << s)) mbar_wait(&sh.kv_full[s], (last_parity >> s) & 1, kErrWaitTimeoutDrain);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      bool issued_any = false;
+      bool ok = mbar_wait(&sh.q_full, 0, kErrWaitTimeoutMma) && !sh.abort;
+      const uint32_t qa = smem_u32(sQ);
+      auto issue_pv = [&](int i) -> bool {
+        const int b = i & 1;
+        const int s = i % ST;
+        if (!mbar_wait(&sh.p_full[b], (i >> 1) & 1, kErrWaitTimeoutMma)) return false;
+        if (!mbar_wait(&sh.o_free[b], ((i >> 1) & 1) ^ 1, kErrWaitTimeoutMma)) return false;
+        if (sh.abort) return false;
+        tc_fence_after();
+        const uint32_t pa = smem_u32(sP + b * P_BYTES);
+        const uint32_t vb = smem_u32(sV + s * V_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / MMA_K; ++kk)
+          mma_f8(tmem + col_o(b), smem_desc_sw128(pa + kk * MMA_K), smem_desc_sw128(vb + kk * MMA_K), IDESC_PV,
+                 kk != 0 ? 1u : 0u);
+        mma_commit(&sh.o_full[b]);
+        mma_commit(&sh.p_free[b]);
+        mma_commit(&sh.kv_empty[s]);
+        return true;
+      };
+      for (int j = 0; ok && j < nk; ++j) {
+        const int s = j % ST;
+        if (!mbar_wait(&sh.kv_full[s], (j / ST) & 1, kErrWaitTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        if (j > 0 && !mbar_wait(&sh.s_free, (j - 1) & 1, kErrWaitTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        if (sh.abort) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t kb = smem_u32(sK + s * K_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / MMA_K; ++kk)
+          mma_i8(tmem + COL_S, smem_desc_sw128(qa + kk * MMA_K), smem_desc_sw128(kb + kk * MMA_K), IDESC_QK,
+                 kk != 0 ? 1u : 0u);
+        issued_any = true;
+        mma_commit(&sh.s_full);
+        if (j > 0 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok && nk > 0) ok = issue_pv(nk - 1);
+      if (!ok) sh.abort = 1;
+      if (issued_any) {
+        mma_commit(&sh.drain);
+        mbar_wait(&sh.drain, 0, kErrWaitTimeoutDrain);
+      }
+    }
+    __syncwarp();
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ softmax
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int64_t qrow = q0 + row;
+    // rows past the end get a positive placeholder scale (their output is never stored)
+    const float qsv = qrow < p.seq ? __ldg(p.qs_t + head * p.seq_pad + qrow) : 1.0f;
+    const float ra = __fmul_rn(__fmul_rn(qsv, p.attn_scale), kLog2e);
+    const uint32_t t_s = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + COL_S;
+    float m = -INFINITY;
+    for (int j = 0; j < nk; ++j) {
+      bool ok = mbar_wait(&sh.s_full, j & 1, kErrWaitTimeoutEpilogue);
+      ok = __all_sync(0xffffffffu, ok) && !sh.abort;
+      if (!ok) {
+        sh.abort = 1;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[128];
+      tmem_ld_32x32b_x32(t_s + 0, *reinterpret_cast<uint32_t(*)[32]>(sr + 0));
+      tmem_ld_32x32b_x32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+      tmem_ld_32x32b_x32(t_s + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
+      tmem_ld_32x32b_x32(t_s + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < 128; c += 32) reg_dep32(*reinterpret_cast<uint32_t(*)[32]>(sr + c));
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.s_free);
+      const int s = j % ST;
+      // the key scales arrived with this stage (the MMA consumed it before committing S)
+      ok = mbar_wait(&sh.kv_full[s], (j / ST) & 1, kErrWaitTimeoutEpilogue);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        sh.abort = 1;
+        break;
+      }
+      const float4* ks4 = reinterpret_cast<const float4*>(sKS + s * KS_BYTES);
+      const int64_t left = p.seq - static_cast<int64_t>(j) * BN;
+      const int valid = left < BN ? static_cast<int>(left) : BN;
+      float y[128];
+#pragma unroll
+      for (int c = 0; c < 128; c += 4) {
+        const float4 k4 = ks4[c / 4];
+        y[c + 0] = __fmul_rn(__int2float_rn(static_cast<int>(sr[c + 0])), k4.x);
+        y[c + 1] = __fmul_rn(__int2float_rn(static_cast<int>(sr[c + 1])), k4.y);
+        y[c + 2] = __fmul_rn(__int2float_rn(static_cast<int>(sr[c + 2])), k4.z);
+        y[c + 3] = __fmul_rn(__int2float_rn(static_cast<int>(sr[c + 3])), k4.w);
+      }
+      if (valid < BN) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) y[c] = c < valid ? y[c] : -INFINITY;
+      }
+      float mx[4] = {y[0], y[1], y[2], y[3]};
+#pragma unroll
+      for (int c = 4; c < 128; c += 8) {
+        mx[0] = fmax3(mx[0], y[c + 0], y[c + 4]);
+        mx[1] = fmax3(mx[1], y[c + 1], y[c + 5]);
+        mx[2] = fmax3(mx[2], y[c + 2], y[c + 6]);
+        mx[3] = fmax3(mx[3], y[c + 3], y[c + 7]);
+      }
+      const float mrow = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
+      const float m_new = fmaxf(m, __fmul_rn(mrow, ra));
+      const float alpha = ex2_approx(__fsub_rn(m, m_new));
+      m = m_new;
+      // hand alpha to the correction warps
+      const int a = j % AR;
+      ok = mbar_wait(&sh.a_free[a], ((j / AR) & 1) ^ 1, kErrWaitTimeoutEpilogue);
+      ok = __all_sync(0xffffffffu, ok) && !sh.abort;
+      if (!ok) {
+        sh.abort = 1;
+        break;
+      }
+      sh.alpha[a][row] = alpha;
+      mbar_arrive(&sh.a_full[a]);
+      // P tile: E4M3, K-major with the 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7))
+      const int b = j & 1;
+      ok = mbar_wait(&sh.p_free[b], ((j >> 1) & 1) ^ 1, kErrWaitTimeoutEpilogue);
+      ok = __all_sync(0xffffffffu, ok) && !sh.abort;
+      if (!ok) {
+        sh.abort = 1;
+        break;
+      }
+      uint8_t* prow = sP + b * P_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
+      const float nm = -m_new;
+#pragma unroll
+      for (int c16 = 0; c16 < 8; ++c16) {
+        uint32_t w[4];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int c = c16 * 16 + q4 * 4;
+          const float e0 = ex2_approx(__fmaf_rn(y[c + 0], ra, nm));
+          const float e1 = ex2_approx(__fmaf_rn(y[c + 1], ra, nm));
+          const float e2 = ex2_approx(__fmaf_rn(y[c + 2], ra, nm));
+          const float e3 = ex2_approx(__fmaf_rn(y[c + 3], ra, nm));
+          const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(e0, e1), __NV_SATFINITE, __NV_E4M3);
+          const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(e2, e3), __NV_SATFINITE, __NV_E4M3);
+          w[q4] = lo | (hi << 16);
+        }
+        *reinterpret_cast<uint4*>(prow + ((c16 ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&sh.p_full[b]);
+    }
+  } else {
+    // ------------------------------------------------------------ correction + output
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    float acc[128];
+#pragma unroll
+    for (int c = 0; c < 128; ++c) acc[c] = 0.0f;
+    float l = 0.0f;
+    bool good = true;
+    for (int i = 0; i < nk; ++i) {
+      const int b = i & 1;
+      const int a = i % AR;
+      bool ok = mbar_wait(&sh.o_full[b], (i >> 1) & 1, kErrWaitTimeoutEpilogue);
+      ok = ok && mbar_wait(&sh.a_full[a], (i / AR) & 1, kErrWaitTimeoutEpilogue);
+      ok = __all_sync(0xffffffffu, ok) && !sh.abort;
+      if (!ok) {
+        sh.abort = 1;
+        good = false;
+        break;
+      }
+      const float alpha = sh.alpha[a][row];
+      mbar_arrive(&sh.a_free[a]);
+      tc_fence_after();
+      const uint32_t t_o = t_lane + col_o(b);
+      uint32_t r0[16], r1[16];
+      tmem_ld_32x32b_x16(t_o + 0, r0);
+      tmem_ld_wait();
+      reg_dep16(r0);
+#pragma unroll
+      for (int c = 0; c < 128; c += 32) {
+        // one load in flight while the previous chunk is accumulated
+        tmem_ld_32x32b_x16(t_o + c + 16, r1);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) acc[c + e] = __fmaf_rn(acc[c + e], alpha, __uint_as_float(r0[e]));
+        tmem_ld_wait();
+        reg_dep16(r1);
+        tmem_ld_32x32b_x16(t_o + c + 32, r0);  // c + 32 == 128 on the last pass: the row-sum column
+#pragma unroll
+        for (int e = 0; e < 16; ++e) acc[c + 16 + e] = __fmaf_rn(acc[c + 16 + e], alpha, __uint_as_float(r1[e]));
+        tmem_ld_wait();
+        reg_dep16(r0);
+      }
+      l = __fmaf_rn(l, alpha, __uint_as_float(r0[0]));
+      tc_fence_before();
+      mbar_arrive(&sh.o_free[b]);
+    }
+    const int64_t qrow = q0 + row;
+    if (good && !sh.abort && qrow < p.seq) {
+      const float vs = v_scale_of(__ldg(p.v_amax));
+      uint4* dst = reinterpret_cast<uint4*>(p.out + qrow * p.ldo + static_cast<int64_t>(head) * D);
+#pragma unroll
+      for (int c = 0; c < 128; c += 8) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float lo = __fdiv_rn(__fmul_rn(acc[c + 2 * e], vs), l);
+          const float hi = __fdiv_rn(__fmul_rn(acc[c + 2 * e + 1], vs), l);
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
+          w[e] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+        dst[c / 8] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+}  // namespace fl
+
+}  // namespace attn
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*PFN_encodeTiledAttn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                        const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                        CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                        CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiledAttn attn_encode_fn() {
+  static PFN_encodeTiledAttn fn = nullptr;
+  if (fn == nullptr) {
+    void* sym = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &sym, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiledAttn>(sym);
+  }
+  return fn;
+}
+
+// 2-D byte matrix [rows, cols] with row pitch `pitch`, box 128 x 128, 128-byte swizzle.
+static bool make_byte_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t pitch) {
+  PFN_encodeTiledAttn enc = attn_encode_fn();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
+  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static int sm_count() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+cudaError_t launch_attn_quant_qk(const void* src, int64_t seq, int64_t seq_pad, int heads, int64_t row_stride,
+                                 int64_t q_off, int64_t k_off, int rotate, int8_t* q, float* qs_t, int8_t* k,
+                                 float* ks_t, cudaStream_t st) {
+  const int64_t warps = (2 * seq_pad * heads + 7) / 8;
+  const int64_t want = (warps + 7) / 8;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+  const int grid = static_cast<int>(want < cap ? want : cap);
+  attn::quant_qk_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), seq, seq_pad, heads, row_stride,
+                                              q_off, k_off, rotate, q, qs_t, k, ks_t);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attn_quant_v(const void* src, int64_t seq, int64_t seq_pad, int heads, int64_t row_stride,
+                                int64_t v_off, uint8_t* v_t, float* v_amax, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(v_amax, 0, sizeof(float), st);
+  if (e != cudaSuccess) return e;
+  const int grid_a = sm_count() * 8;
+  attn::v_amax_kernel<<<grid_a, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), seq, heads, row_stride, v_off,
+                                               v_amax);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  attn::quant_v_kernel<<<dim3(static_cast<unsigned>(seq_pad / 128), static_cast<unsigned>(heads)), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(src), seq, seq_pad, heads, row_stride, v_off, v_amax, v_t);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attn_flash(const int8_t* q, const float* qs_t, const int8_t* k, const float* ks_t,
+                              const uint8_t* v_t, const float* v_amax, float attn_scale, int64_t seq, int heads,
+                              int64_t seq_pad, void* out, int64_t ldo, cudaStream_t st) {
+  namespace F = attn::fl;
+  CUtensorMap mq, mk, mv;
+  const int64_t hd = static_cast<int64_t>(heads) * attn::D;
+  if (!make_byte_map(&mq, q, seq, hd, hd) || !make_byte_map(&mk, k, seq, hd, hd) ||
+      !make_byte_map(&mv, v_t, hd, seq_pad, seq_pad))
+    return cudaErrorInvalidValue;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool attr_set[64] = {false};
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(F::flash_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(F::SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  F::Params p{qs_t, ks_t, v_amax, static_cast<__nv_bfloat16*>(out), ldo, seq, seq_pad, attn_scale};
+  const dim3 grid(static_cast<unsigned>((seq + F::BM - 1) / F::BM), static_cast<unsigned>(heads));
+  F::flash_kernel<<<grid, F::THREADS, F::SMEM_BYTES, st>>>(mq, mk, mv, p);
+  return cudaGetLastError();
+}
+
+}  // namespace slim
+
+// ------------------------------------------------------------------ C ABI
+using namespace slim;
+
+namespace {
+
+constexpr int64_t kAttnAlign = 256;
+
+int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+int attn_shape_checks(int64_t seq, int heads, int dim) {
+  if (dim != attn::D) return fail(SLIM_ERR_SHAPE, "attention kernel supports head dim 128, got %d", dim);
+  if (heads <= 0 || seq < 0) return fail(SLIM_ERR_SHAPE, "bad attention shape seq=%lld heads=%d", static_cast<long long>(seq), heads);
+  if (seq >= (int64_t{1} << 31) || static_cast<int64_t>(heads) * dim >= (int64_t{1} << 31))
+    return fail(SLIM_ERR_SHAPE, "attention shape too large");
+  return SLIM_OK;
+}
+
+int seq_pad_check(int64_t seq, int64_t seq_pad) {
+  if (seq_pad % 128 != 0 || seq_pad < round_up(seq, 128))
+    return fail(SLIM_ERR_SHAPE, "seq_pad must be a multiple of 128 and >= seq rounded up to 128, got %lld for seq %lld",
+                static_cast<long long>(seq_pad), static_cast<long long>(seq));
+  return SLIM_OK;
+}
+
+struct AttnWorkspace {
+  int64_t q, k, v_t, qs_t, ks_t, amax, total;
+};
+
+AttnWorkspace attn_workspace(int64_t seq, int heads) {
+  const int64_t hd = static_cast<int64_t>(heads) * attn::D;
+  const int64_t seq_pad = round_up(seq, 128);
+  AttnWorkspace w{};
+  int64_t off = 0;
+  w.q = off;
+  off = round_up(off + seq * hd, kAttnAlign);
+  w.k = off;
+  off = round_up(off + seq * hd, kAttnAlign);
+  w.v_t = off;
+  off = round_up(off + hd * seq_pad, kAttnAlign);
+  w.qs_t = off;
+  off = round_up(off + heads * seq_pad * 4, kAttnAlign);
+  w.ks_t = off;
+  off = round_up(off + heads * seq_pad * 4, kAttnAlign);
+  w.amax = off;
+  off = round_up(off + 4, kAttnAlign);
+  w.total = off;
+  return w;
+}
+
+}  // namespace
+
+extern "C" {
+
+int slim_attn_workspace_bytes(int64_t seq, int heads, int dim, uint64_t* bytes) {
+  int rc;
+  if ((rc = attn_shape_checks(seq, heads, dim)) != SLIM_OK) return rc;
+  if (bytes == nullptr) return fail(SLIM_ERR_NULL, "bytes is NULL");
+  *bytes = static_cast<uint64_t>(attn_workspace(seq, heads).total);
+  return SLIM_OK;
+}
+
+int slim_attn_quant_qk(const void* qkv, int64_t seq, int heads, int dim, int64_t row_stride, int64_t q_offset,
+                       int64_t k_offset, int rotate, int8_t* q, float* q_scale_t, int8_t* k, float* k_scale_t,
+                       int64_t seq_pad, void* stream) {
+  int rc;
+  if ((rc = attn_shape_checks(seq, heads, dim)) != SLIM_OK) return rc;
+  if ((rc = seq_pad_check(seq, seq_pad)) != SLIM_OK) return rc;
+  if (seq == 0) return SLIM_OK;
+  if (qkv == nullptr || q == nullptr || q_scale_t == nullptr || k == nullptr || k_scale_t == nullptr)
+    return fail(SLIM_ERR_NULL, "qkv/q/q_scale_t/k/k_scale_t is NULL");
+  if (row_stride < static_cast<int64_t>(heads) * dim || q_offset < 0 || k_offset < 0)
+    return fail(SLIM_ERR_SHAPE, "bad row stride / offsets");
+  if (!aligned16(qkv) || (row_stride % 8) || (q_offset % 8) || (k_offset % 8) || !aligned16(q) || !aligned16(k))
+    return fail(SLIM_ERR_ALIGN, "qkv rows, offsets and the int8 outputs must be 16-byte aligned");
+  if ((rc = check_arch()) != SLIM_OK) return rc;
+  cudaError_t e = launch_attn_quant_qk(qkv, seq, seq_pad, heads, row_stride, q_offset, k_offset, rotate, q, q_scale_t,
+                                       k, k_scale_t, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attention q/k quantiser launch");
+  note_launch();
+  return SLIM_OK;
+}
+
+int slim_attn_quant_v(const void* qkv, int64_t seq, int heads, int dim, int64_t row_stride, int64_t v_offset,
+                      uint8_t* v_t, int64_t seq_pad, float* v_amax, void* stream) {
+  int rc;
+  if ((rc = attn_shape_checks(seq, heads, dim)) != SLIM_OK) return rc;
+  if ((rc = seq_pad_check(seq, seq_pad)) != SLIM_OK) return rc;
+  if (seq == 0) return SLIM_OK;
+  if (qkv == nullptr || v_t == nullptr || v_amax == nullptr) return fail(SLIM_ERR_NULL, "qkv/v_t/v_amax is NULL");
+  if (row_stride < static_cast<int64_t>(heads) * dim || v_offset < 0) return fail(SLIM_ERR_SHAPE, "bad row stride / offset");
+  if (!aligned16(qkv) || (row_stride % 8) || (v_offset % 8) || !aligned16(v_t) ||
+      (reinterpret_cast<uintptr_t>(v_amax) & 3u))
+    return fail(SLIM_ERR_ALIGN, "qkv rows, offset and v_t must be 16-byte aligned");
+  if ((rc = check_arch()) != SLIM_OK) return rc;
+  cudaError_t e = launch_attn_quant_v(qkv, seq, seq_pad, heads, row_stride, v_offset, v_t, v_amax,
+                                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attention v quantiser launch");
+  note_launch(2);
+  return SLIM_OK;
+}
+
+int slim_attn_int8(const int8_t* q, const float* q_scale_t, const int8_t* k, const float* k_scale_t,
+                   const uint8_t* v_t, const float* v_amax, float attn_scale, int64_t seq, int heads, int dim,
+                   int64_t seq_pad, void* out, int64_t ldo, void* stream) {
+  int rc;
+  if ((rc = attn_shape_checks(seq, heads, dim)) != SLIM_OK) return rc;
+  if ((rc = seq_pad_check(seq, seq_pad)) != SLIM_OK) return rc;
+  if (seq == 0) return SLIM_OK;
+  if (q == nullptr || q_scale_t == nullptr || k == nullptr || k_scale_t == nullptr || v_t == nullptr ||
+      v_amax == nullptr || out == nullptr)
+    return fail(SLIM_ERR_NULL, "q/q_scale_t/k/k_scale_t/v_t/v_amax/out is NULL");
+  if (ldo < static_cast<int64_t>(heads) * dim) return fail(SLIM_ERR_SHAPE, "ldo smaller than heads * dim");
+  if (!(attn_scale > 0.0f)) return fail(SLIM_ERR_SHAPE, "attn_scale must be positive");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v_t) || !aligned16(k_scale_t) || !aligned16(out) || (ldo % 8))
+    return fail(SLIM_ERR_ALIGN, "q/k/v_t/k_scale_t/out must be 16-byte aligned and ldo a multiple of 8");
+  if ((rc = check_arch()) != SLIM_OK) return rc;
+  cudaError_t e = launch_attn_flash(q, q_scale_t, k, k_scale_t, v_t, v_amax, attn_scale, seq, heads, seq_pad, out, ldo,
+                                    static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attention kernel launch");
+  note_launch();
+  return SLIM_OK;
+}
+
+int slim_attn_packed(const void* qkv, int64_t seq, int heads, int dim, int rotate, void* out, void* workspace,
+                     uint64_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = attn_shape_checks(seq, heads, dim)) != SLIM_OK) return rc;
+  if (seq == 0) return SLIM_OK;
+  if (qkv == nullptr || out == nullptr || workspace == nullptr) return fail(SLIM_ERR_NULL, "qkv/out/workspace is NULL");
+  const AttnWorkspace w = attn_workspace(seq, heads);
+  if (workspace_bytes < static_cast<uint64_t>(w.total))
+    return fail(SLIM_ERR_SHAPE, "workspace of %llu bytes is smaller than the %lld needed",
+                static_cast<unsigned long long>(workspace_bytes), static_cast<long long>(w.total));
+  if (!aligned16(workspace)) return fail(SLIM_ERR_ALIGN, "workspace must be 16-byte aligned");
+  const int64_t hd = static_cast<int64_t>(heads) * dim;
+  const int64_t seq_pad = round_up(seq, 128);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int8_t* q = reinterpret_cast<int8_t*>(ws + w.q);
+  int8_t* k = reinterpret_cast<int8_t*>(ws + w.k);
+  uint8_t* v_t = ws + w.v_t;
+  float* qs_t = reinterpret_cast<float*>(ws + w.qs_t);
+  float* ks_t = reinterpret_cast<float*>(ws + w.ks_t);
+  float* amax = reinterpret_cast<float*>(ws + w.amax);
+  if ((rc = slim_attn_quant_qk(qkv, seq, heads, dim, 3 * hd, 0, hd, rotate, q, qs_t, k, ks_t, seq_pad, stream)) != SLIM_OK)
+    return rc;
+  if ((rc = slim_attn_quant_v(qkv, seq, heads, dim, 3 * hd, 2 * hd, v_t, seq_pad, amax, stream)) != SLIM_OK) return rc;
+  const float scale = static_cast<float>(1.0 / __builtin_sqrt(static_cast<double>(dim)) / (rotate ? dim : 1));
+  return slim_attn_int8(q, qs_t, k, ks_t, v_t, amax, scale, seq, heads, dim, seq_pad, out, hd, stream);
+}
+
+}  // extern "C"

@@ -196,6 +196,17 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Placed right after tmem_ld_wait(): makes every later use of the registers depend on this
+// point, so the compiler cannot move their consumers above the wait.
+__device__ __forceinline__ void reg_dep16(uint32_t (&r)[16]) {
+  asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+               "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]));
+}
+__device__ __forceinline__ void reg_dep32(uint32_t (&r)[32]) {
+  reg_dep16(*reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+  reg_dep16(*reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+}
+
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA with the
 // 128-byte swizzle: rows of 128 bytes, 8-row core groups 1024 bytes apart.
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
@@ -330,6 +341,46 @@ __device__ __forceinline__ void mma_i8_pair(uint32_t tmem_d, uint64_t adesc, uin
 __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_addr) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
                : "memory");
+}
+
+// ---------------------------------------------------------------- FP8 (kind::f8f6f4)
+// Instruction descriptor for kind::f8f6f4 with A and B both E4M3 (format code 0), fp32
+// accumulator, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_f8_e4m3(int m, int n) {
+  return (1u << 4)                                   // D format: F32
+         | (static_cast<uint32_t>(n >> 3) << 17)     // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, E4M3 x E4M3 -> fp32, K = 32 per instruction, one CTA.
+__device__ __forceinline__ void mma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy reads
+// (tensor-core operands written by threads instead of TMA).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Hardware base-2 exponential (PTX ex2.approx.ftz.f32; -inf -> +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// max(a, b, c) in one instruction (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float y;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+  return y;
 }
 
 __device__ __forceinline__ bool elect_one() {

@@ -8,3 +8,4 @@
 #include "gemm_nvf4.cu"
 #include "capi_nvfp4.cu"
 #include "verify.cu"
+#include "attn.cu"

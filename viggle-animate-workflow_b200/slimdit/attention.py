@@ -1,0 +1,309 @@
+"""In-place INT8/FP8 flash attention for the Viggle / MiniMax-H3 DiT on sm_100a.
+
+Drop-in for the reference's comfyui/ComfyUI-SlimDiT/attention_triton.py: the same public
+names (``packed_geometry``, ``unwrap``, ``TritonAttnConfig``, ``TritonAttnOverride``,
+``install_triton_attn``) and the same dispatch rules, with the Triton kernels replaced by the
+tcgen05 kernels of libslimdit_b200 (``slim_attn_*``):
+
+    Q, K  int8, one scale per (token, head), after the +-1 Sylvester Hadamard (``rotate``)
+    V     E4M3 with one global scale
+    QK    tcgen05 kind::i8, int32 in tensor memory; PV tcgen05 kind::f8f6f4, fp32
+
+The packed [S, 3*H*D] bf16 buffer the DiT splits into q/k/v views is read in place
+(attention_triton.py:185-222); no contiguous copies are made. Calls the kernel cannot take
+(a mask, a layout other than the packed views, a head dim other than 128, a sequence shorter
+than ``min_seq``) go back to the model's own attention, as in the reference
+(attention_triton.py:253-263, 301-305). There is no CPU path: ``attention_packed`` raises
+``NativeUnavailable`` without the library and an sm_100 GPU.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import time
+
+DEFAULT_MIN_SEQ = 12000  # below this the dense path wins outright (attention_triton.py:34)
+# The sm_100a kernel has one geometry: 128 query rows x 128 keys per step, 10 warps, a 3-deep
+# K/V ring. The fields are kept so callers that set them still work; the kernel ignores them.
+DEFAULT_BLOCK_M = 128
+DEFAULT_BLOCK_N = 128
+DEFAULT_WARPS = 10
+DEFAULT_STAGES = 3
+QUANT_BLOCK = 64
+HEAD_DIM = 128  # the one head dim the kernel supports (MiniMax-H3: 56 heads x 128)
+
+
+def unwrap(value):
+    """Mirror ``attention_ops._tensor`` (attention_triton.py:177-187): an
+    ``AttentionTensorContainer`` is single-owner and ``take()`` returns and consumes the tensor.
+    Plain tensors also expose ``take()``, so a tensor is recognised by its own interface first."""
+    if hasattr(value, "data_ptr") and hasattr(value, "stride"):
+        return value
+    take = getattr(value, "take", None)
+    return take() if take is not None else value
+
+
+def packed_geometry(q, k, v, heads):
+    """Validate the packed (seq, 3*heads*dim) layout (attention_triton.py:190-222) and return what
+    the kernel needs, or None.
+
+    q, k and v must be (1, heads, seq, dim) bf16 views of one buffer: q at offset 0, k at
+    heads*dim, v at 2*heads*dim, every row 3*heads*dim elements long."""
+    if q is None or k is None or v is None:
+        return None
+    shape = getattr(q, "shape", None)
+    if shape is None or len(shape) != 4 or tuple(shape) != tuple(k.shape) or tuple(shape) != tuple(v.shape):
+        return None
+    batch, dim_heads, seq, dim = shape
+    if batch != 1 or dim_heads != heads or seq <= 0 or dim <= 0 or (dim & (dim - 1)):
+        return None
+    if not (q.dtype == k.dtype == v.dtype) or "bfloat16" not in str(q.dtype):
+        return None
+    if q.stride(3) != 1 or q.stride(2) != 3 * dim_heads * dim or q.stride(1) != dim:
+        return None
+    if (k.stride(3), k.stride(2), k.stride(1)) != (1, 3 * dim_heads * dim, dim):
+        return None
+    if (v.stride(3), v.stride(2), v.stride(1)) != (1, 3 * dim_heads * dim, dim):
+        return None
+    row_bytes = dim_heads * dim * q.element_size()
+    if k.data_ptr() - q.data_ptr() != row_bytes or v.data_ptr() - q.data_ptr() != 2 * row_bytes:
+        return None
+    return {"seq": seq, "heads": dim_heads, "dim": dim, "row_stride": 3 * dim_heads * dim,
+            "head_stride": dim, "row_bytes": row_bytes}
+
+
+def attn_scale(dim: int, rotate: bool) -> float:
+    """The unnormalised Hadamard makes (qH).(kH)^T = dim * q.k^T, so the scale carries 1/dim
+    (attention_triton.py:296-298)."""
+    return dim ** -0.5 / (dim if rotate else 1.0)
+
+
+def workspace_bytes(seq: int, heads: int, dim: int = HEAD_DIM) -> int:
+    from . import _native as nat
+
+    out = ctypes.c_uint64(0)
+    nat.check(nat.load().slim_attn_workspace_bytes(int(seq), int(heads), int(dim), ctypes.byref(out)))
+    return int(out.value)
+
+
+def attention_packed(qkv, heads: int, rotate: bool = True, out=None, workspace=None):
+    """Attention over a packed [seq, 3*heads*128] bf16 CUDA buffer (rows may be longer: the row
+    pitch is taken from the tensor's stride) -> bf16 [seq, heads*128].
+
+    The device entry point behind ``TritonAttnOverride``: quantise q/k (int8 per token and
+    head, rotated) and v (E4M3, global scale), then the tcgen05 flash kernel."""
+    from . import _native as nat
+
+    torch = nat.require_cuda()
+    if qkv.dim() != 2 or qkv.dtype != torch.bfloat16 or not qkv.is_cuda or qkv.stride(1) != 1:
+        raise ValueError("qkv must be a CUDA bf16 [seq, 3*heads*dim] tensor with unit column stride")
+    seq, width = qkv.shape
+    hd = heads * HEAD_DIM
+    if width != 3 * hd:
+        raise ValueError(f"qkv has {width} columns; {heads} heads of dim {HEAD_DIM} need {3 * hd}")
+    lib = nat.load()
+    dev = qkv.device
+    if out is None:
+        out = torch.empty((seq, hd), dtype=torch.bfloat16, device=dev)
+    if seq == 0:
+        return out
+    if out.shape != (seq, hd) or out.dtype != torch.bfloat16 or out.stride(1) != 1:
+        raise ValueError("out must be bf16 [seq, heads*dim] with unit column stride")
+    need = workspace_bytes(seq, heads)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty((need,), dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    row_stride = qkv.stride(0)
+    if row_stride == 3 * hd and out.stride(0) == hd:
+        nat.check(lib.slim_attn_packed(qkv.data_ptr(), seq, heads, HEAD_DIM, int(bool(rotate)), out.data_ptr(),
+                                       workspace.data_ptr(), need, st))
+        return out
+    # general row pitches: the three stages with the packed entry's workspace layout
+    parts = _workspace_views(workspace, seq, heads)
+    nat.check(lib.slim_attn_quant_qk(qkv.data_ptr(), seq, heads, HEAD_DIM, row_stride, 0, hd, int(bool(rotate)),
+                                     parts["q"], parts["qs"], parts["k"], parts["ks"], parts["seq_pad"], st))
+    nat.check(lib.slim_attn_quant_v(qkv.data_ptr(), seq, heads, HEAD_DIM, row_stride, 2 * hd, parts["v"],
+                                    parts["seq_pad"], parts["amax"], st))
+    nat.check(lib.slim_attn_int8(parts["q"], parts["qs"], parts["k"], parts["ks"], parts["v"], parts["amax"],
+                                 attn_scale(HEAD_DIM, rotate), seq, heads, HEAD_DIM, parts["seq_pad"],
+                                 out.data_ptr(), out.stride(0), st))
+    return out
+
+
+def _workspace_views(workspace, seq: int, heads: int) -> dict:
+    """Byte offsets of the quantised operands inside a slim_attn_packed workspace."""
+    def up(v, a=256):
+        return (v + a - 1) // a * a
+
+    hd = heads * HEAD_DIM
+    seq_pad = up(seq, 128)
+    base = workspace.data_ptr()
+    off = {}
+    o = 0
+    for name, size in (("q", seq * hd), ("k", seq * hd), ("v", hd * seq_pad), ("qs", heads * seq_pad * 4),
+                       ("ks", heads * seq_pad * 4), ("amax", 4)):
+        off[name] = base + o
+        o = up(o + size)
+    off["seq_pad"] = seq_pad
+    return off
+
+
+def quantized_operands(qkv, heads: int, rotate: bool = True) -> dict:
+    """The quantiser stage alone (test and inspection hook): int8 q/k [seq, heads*128], their
+    scales [heads, seq_pad], v as E4M3 bits [heads, 128, seq_pad] and max|v|."""
+    from . import _native as nat
+
+    torch = nat.require_cuda()
+    seq = qkv.shape[0]
+    hd = heads * HEAD_DIM
+    seq_pad = (seq + 127) // 128 * 128
+    dev = qkv.device
+    q = torch.empty((seq, hd), dtype=torch.int8, device=dev)
+    k = torch.empty((seq, hd), dtype=torch.int8, device=dev)
+    qs = torch.empty((heads, seq_pad), dtype=torch.float32, device=dev)
+    ks = torch.empty((heads, seq_pad), dtype=torch.float32, device=dev)
+    v = torch.empty((heads, HEAD_DIM, seq_pad), dtype=torch.uint8, device=dev)
+    amax = torch.empty((1,), dtype=torch.float32, device=dev)
+    lib = nat.load()
+    st = torch.cuda.current_stream(dev).cuda_stream
+    nat.check(lib.slim_attn_quant_qk(qkv.data_ptr(), seq, heads, HEAD_DIM, qkv.stride(0), 0, hd, int(bool(rotate)),
+                                     q.data_ptr(), qs.data_ptr(), k.data_ptr(), ks.data_ptr(), seq_pad, st))
+    nat.check(lib.slim_attn_quant_v(qkv.data_ptr(), seq, heads, HEAD_DIM, qkv.stride(0), 2 * hd, v.data_ptr(), seq_pad,
+                                    amax.data_ptr(), st))
+    return {"q": q, "q_scale": qs, "k": k, "k_scale": ks, "v": v, "v_amax": amax, "seq_pad": seq_pad}
+
+
+def attention_quantized(ops: dict, seq: int, heads: int, scale: float, out=None):
+    """The flash kernel alone on ``quantized_operands`` output -> bf16 [seq, heads*128]."""
+    from . import _native as nat
+
+    torch = nat.require_cuda()
+    dev = ops["q"].device
+    hd = heads * HEAD_DIM
+    if out is None:
+        out = torch.empty((seq, hd), dtype=torch.bfloat16, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    nat.check(nat.load().slim_attn_int8(ops["q"].data_ptr(), ops["q_scale"].data_ptr(), ops["k"].data_ptr(),
+                                        ops["k_scale"].data_ptr(), ops["v"].data_ptr(), ops["v_amax"].data_ptr(),
+                                        float(scale), seq, heads, HEAD_DIM, ops["seq_pad"], out.data_ptr(),
+                                        out.stride(0), st))
+    return out
+
+
+class TritonAttnConfig:
+    """Knobs of the override (attention_triton.py:225-245). ``block_m``/``block_n``/``num_warps``/
+    ``num_stages`` are accepted for compatibility; the sm_100a kernel has one fixed geometry."""
+
+    def __init__(self, enabled=False, block_m=DEFAULT_BLOCK_M, block_n=DEFAULT_BLOCK_N,
+                 num_warps=DEFAULT_WARPS, num_stages=DEFAULT_STAGES, min_seq=DEFAULT_MIN_SEQ,
+                 fail_closed=False, rotate=True):
+        self.enabled = enabled
+        self.block_m = block_m
+        self.block_n = block_n
+        self.num_warps = num_warps
+        self.num_stages = num_stages
+        self.min_seq = min_seq
+        self.fail_closed = fail_closed
+        self.rotate = rotate
+
+    def describe(self):
+        return {"block_m": self.block_m, "block_n": self.block_n, "num_warps": self.num_warps,
+                "num_stages": self.num_stages, "min_seq": self.min_seq, "rotate": self.rotate}
+
+
+class TritonAttnOverride:
+    """Replaces ``comfy.ldm.minimax.model.optimized_attention`` while installed
+    (attention_triton.py:248-305)."""
+
+    def __init__(self, config, stats=None):
+        if not config.enabled:
+            raise ValueError("TritonAttnOverride requires an enabled config")
+        self.config = config
+        self.stats = stats if stats is not None else {}
+        for key in ("calls", "kernel_calls", "fallback_calls",
+                    "quantise_dispatch_seconds", "kernel_dispatch_seconds"):
+            self.stats.setdefault(key, 0 if key.endswith("calls") else 0.0)
+        self._module = None
+        self._original = None
+        self._workspace = {}
+
+    def install(self):
+        import importlib
+
+        module = importlib.import_module("comfy.ldm.minimax.model")
+        self._module = module
+        self._original = module.optimized_attention
+        try:
+            from . import _native
+
+            _native.load()
+            _native.require_cuda()
+        except Exception as exc:  # environment dependent: no library or no sm_100 device
+            if self.config.fail_closed:
+                raise RuntimeError(f"sm_100a attention unavailable: {exc}") from exc
+            print(f"[slim-attn] disabled, kernel unavailable: {exc}", flush=True)
+            return self
+        module.optimized_attention = self
+        return self
+
+    def uninstall(self):
+        if self._module is not None and self._module.optimized_attention is self:
+            self._module.optimized_attention = self._original
+
+    def __call__(self, q, k, v, heads, mask=None, skip_reshape=False, skip_output_reshape=False, **kwargs):
+        started = time.perf_counter()
+        self.stats["calls"] += 1
+        q_t, k_t, v_t = unwrap(q), unwrap(k), unwrap(v)
+        geometry = None
+        if mask is None and skip_reshape:
+            geometry = packed_geometry(q_t, k_t, v_t, heads)
+            if geometry is not None and (geometry["seq"] < self.config.min_seq or geometry["dim"] != HEAD_DIM):
+                geometry = None
+        if geometry is None:
+            return self._fallback(q_t, k_t, v_t, heads, mask, skip_reshape, skip_output_reshape, kwargs, started)
+
+        out = self._run(q_t, k_t, v_t, geometry)
+        self.stats["kernel_calls"] += 1
+        if skip_output_reshape:
+            # same contract as the Sol-Attn override: (1, heads, seq, dim)
+            return out.view(1, geometry["seq"], heads, geometry["dim"]).transpose(1, 2)
+        return out.reshape(1, geometry["seq"], heads * geometry["dim"])
+
+    def _run(self, q, k, v, geometry):
+        import torch
+
+        seq, heads, dim = geometry["seq"], geometry["heads"], geometry["dim"]
+        started = time.perf_counter()
+        # q is the packed buffer's first column block: a [seq, 3*heads*dim] view starting at q
+        qkv = torch.as_strided(q, (seq, 3 * heads * dim), (geometry["row_stride"], 1), q.storage_offset())
+        need = workspace_bytes(seq, heads, dim)
+        ws = self._workspace.get(q.device)
+        if ws is None or ws.numel() < need:
+            ws = torch.empty((need,), dtype=torch.uint8, device=q.device)
+            self._workspace[q.device] = ws
+        out = torch.empty((seq, heads * dim), dtype=torch.bfloat16, device=q.device)
+        self.stats["quantise_dispatch_seconds"] += time.perf_counter() - started
+        started = time.perf_counter()
+        attention_packed(qkv, heads, rotate=self.config.rotate, out=out, workspace=ws)
+        self.stats["kernel_dispatch_seconds"] += time.perf_counter() - started
+        return out.unsqueeze(0)
+
+    def _fallback(self, q, k, v, heads, mask, skip_reshape, skip_output_reshape, kwargs, started):
+        out = self._original(q, k, v, heads, mask=mask, skip_reshape=skip_reshape,
+                             skip_output_reshape=skip_output_reshape, **kwargs)
+        self.stats["fallback_calls"] += 1
+        return out
+
+
+def install_triton_attn(config=None, stats=None):
+    """Install the sm_100a kernel for every length (the reference's ``VIGGLE_ATTN=triton``)."""
+    config = config if config is not None else TritonAttnConfig(enabled=True)
+    if not config.enabled:
+        return None
+    return TritonAttnOverride(config, stats).install()
+
+
+__all__ = [
+    "DEFAULT_MIN_SEQ", "HEAD_DIM", "TritonAttnConfig", "TritonAttnOverride", "attention_packed", "attention_quantized",
+    "attn_scale", "install_triton_attn", "packed_geometry", "quantized_operands", "unwrap", "workspace_bytes",
+]
