@@ -255,6 +255,17 @@ int slim_attn_quant_v(const void* qkv, int64_t seq, int heads, int dim, int64_t 
                       int64_t v_offset, uint8_t* v_t, int64_t seq_pad, float* v_amax,
                       void* stream);
 
+/* The two halves of slim_attn_quant_v, for callers that split the heads over several GPUs:
+ * the V scale is global over all heads (attention_triton.py:283-286), so each GPU computes the
+ * amax of its own heads, the maxima are reduced (one float), and every GPU quantises its heads
+ * with the common amax. slim_attn_v_amax writes max|v| of the given heads to *v_amax;
+ * slim_attn_quant_v_scaled quantises with the given *v_amax. */
+int slim_attn_v_amax(const void* qkv, int64_t seq, int heads, int dim, int64_t row_stride,
+                     int64_t v_offset, float* v_amax, void* stream);
+int slim_attn_quant_v_scaled(const void* qkv, int64_t seq, int heads, int dim,
+                             int64_t row_stride, int64_t v_offset, uint8_t* v_t,
+                             int64_t seq_pad, const float* v_amax, void* stream);
+
 /* out[seq, ldo] bf16 (head h at columns [h*dim, h*dim+dim)) = softmax attention of the
  * quantised q/k/v above with logits s * q_scale * k_scale * attn_scale, P rounded to E4M3
  * for both P V and the row sum (flash_int8, attention_triton.py:131-174). */

@@ -104,9 +104,11 @@ def attn_scale(dim: int, rotate: bool) -> np.float32:
 
 def flash(q8: np.ndarray, qs: np.ndarray, k8: np.ndarray, ks: np.ndarray, v8: np.ndarray, amax: np.float32,
           scale: np.float32) -> np.ndarray:
-    """Online-softmax attention over 128-key tiles. q8/k8 int8 [S, H, D], qs/ks [S, H], v8 e4m3
-    bits [S, H, D]. Returns fp32 values of the bf16 output [S, H, D]."""
+    """Online-softmax attention over 128-key tiles. q8 int8 [Sq, H, D] with qs [Sq, H]; k8 int8
+    [S, H, D] with ks [S, H]; v8 e4m3 bits [S, H, D] (Sq may be a leading subset of the S query
+    rows). Returns fp32 values of the bf16 output [Sq, H, D]."""
     s_len, heads, dim = q8.shape
+    n_keys = k8.shape[0]
     vs = v_scale_of(amax)
     vv = e4m3_decode(v8).astype(np.float64)
     out = np.empty((s_len, heads, dim), dtype=np.float32)
@@ -116,8 +118,8 @@ def flash(q8: np.ndarray, qs: np.ndarray, k8: np.ndarray, ks: np.ndarray, v8: np
         m = np.full(s_len, -np.inf, dtype=np.float32)
         acc = np.zeros((s_len, dim), dtype=np.float32)
         l = np.zeros(s_len, dtype=np.float32)
-        for k0 in range(0, s_len, TILE_KEYS):
-            k1 = min(k0 + TILE_KEYS, s_len)
+        for k0 in range(0, n_keys, TILE_KEYS):
+            k1 = min(k0 + TILE_KEYS, n_keys)
             # integer dot products of int8 codes: |s| < 2^22, exact in fp64 and in fp32
             sc = (qi @ k8[k0:k1, h].astype(np.float64).T).astype(np.float32)
             y = (sc * ks[k0:k1, h].astype(np.float32)[None, :]).astype(np.float32)

@@ -3,7 +3,9 @@
 * output-column split (slimdit/colsplit.py): each rank computes its column block with the
   CUDA linear and NCCL all-gathers them, or (PeerColumnSplit) its GEMM epilogue stores the
   tiles into every rank's output over NVLink; either way the result must equal, bit for bit,
-  the single-GPU linear on the full weight computed on the same rank.
+  the single-GPU linear on the full weight computed on the same rank;
+* attention with the heads split over the ranks (slimdit.attention.attention_heads) equals the
+  single-GPU attention of those heads (the V amax all-reduced).
 """
 
 import os
@@ -65,6 +67,20 @@ def _worker(rank, world, port, result_dir):
                                 assert torch.equal(y[g], full[:mm, g * n // world:(g + 1) * n // world]), (mode, layout)
                 finally:
                     fused.close()
+        # attention with the heads split over the ranks: the V amax is all-reduced, so each rank's
+        # heads equal the single-GPU result bit for bit
+        from slimdit import attention
+        seq, heads = 700, 4
+        g = torch.Generator(device=dev)
+        g.manual_seed(5)
+        qkv = (torch.randn((seq, 3 * heads * 128), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        qkv[:, 2 * heads * 128 + 3] *= 4.0  # the largest |v| sits in head 0: rank 1 needs the all-reduced amax
+        dist.broadcast(qkv, src=0)          # every rank attends over the same buffer
+        whole = attention.attention_packed(qkv, heads)
+        mine = attention.attention_heads(qkv, heads, rank, world)
+        torch.cuda.synchronize(dev)
+        hl = heads // world
+        assert torch.equal(mine, whole[:, rank * hl * 128:(rank + 1) * hl * 128])
         assert _native.device_error() == 0
         Path(result_dir, f"ok{rank}").write_text("ok")
     finally:

@@ -16,22 +16,26 @@
 //   quant_v_kernel    v / max(amax / 448, 1e-8) rounded to E4M3 (nearest even, saturating;
 //                     :117-129), written transposed per head as [H, D, S_pad] so that the PV
 //                     product reads V as a K-major operand.
-//   flash_kernel      one CTA per (128-query tile, head), 10 warps (flash_int8, :131-174):
+//   flash_kernel      one CTA per (128-query tile, head), 14 warps (flash_int8, :131-174):
 //     warp 0       TMA producer: Q tile once; per key tile the K tile (128 keys x 128 B), the
 //                  V^T tile (128 value columns x 128 keys) and 128 key scales (bulk copy) into
 //                  a 3-stage ring.
-//     warp 1       TMEM (512 columns: S int32 [0,128), O buffers at 128 and 288) and one lane
-//                  issuing the MMAs: S = Q K^T (kind::i8, M=N=128) and O_j = P_j V_j
-//                  (kind::f8f6f4 E4M3, M=128, N=144). V's smem tile carries 16 extra rows,
-//                  the first all ones: column 128 of O_j is the row sum of the FP8-rounded
-//                  P_j, i.e. the reference's l increment, from the same tensor-core pass.
-//     warps 2..5   softmax, one query row per thread: S row from TMEM, y = float(s) * ks,
-//                  running max, alpha = 2^(m - m'), p = 2^(y*ra - m') with the hardware ex2,
-//                  E4M3 pairs written into a 128-byte-swizzled P tile (the PV A operand).
-//     warps 6..9   correction, one row per thread: acc = acc * alpha + O_j, l likewise,
-//                  from double-buffered O tiles; finally out = bf16(acc * v_scale / l).
-//   The MMA lane issues S_{j+1} before P_j V_j, so the softmax of tile j+1 never waits for
-//   the PV product of tile j. Every mbarrier wait is bounded (slim_ptx.cuh).
+//     warp 1       TMEM (S int32 double-buffered at columns 0 and 128, O fp32 at 256) and one
+//                  lane issuing the MMAs: S_j = Q K_j^T (kind::i8, M=N=128) and O += P_j V_j
+//                  (kind::f8f6f4 E4M3, M=128, N=144). V's smem tile carries 16 extra rows, the
+//                  first all ones: column 128 of O accumulates the row sum of the FP8-rounded
+//                  P, i.e. the reference's l, in the same tensor-core pass.
+//     warps 2..9   softmax, two warps per TMEM lane quarter, each one query row x 64 keys:
+//                  y = float(s) * ks (exact int-to-float on the integer and FMA pipes), the
+//                  row maximum over both halves (bounded mbarrier exchange), alpha =
+//                  2^(m - m'), p = 2^(y*ra - m') with the hardware ex2, E4M3 pairs written into
+//                  a 128-byte-swizzled P tile (the PV A operand).
+//     warps 10..13 correction, one row each: O *= alpha in TMEM between two PV products (the
+//                  reference's acc * alpha before dot(p, v, acc)), skipped by a warp whose 32
+//                  alphas are exactly 1; finally out = bf16(O * v_scale / l).
+//   The MMA lane issues S_{j+1} before P_j V_j. The softmax is bound by instruction issue
+//   (about 7 instructions per score: int-to-float 2, scale 1, max 0.5, exponent argument 1,
+//   ex2 1, E4M3 pack 0.75); every mbarrier wait is bounded (slim_ptx.cuh).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
@@ -223,11 +227,13 @@ constexpr int VT_BYTES = D * BN;  // the TMA part of a V stage
 constexpr int V_BYTES = NV * BN;
 constexpr int KS_BYTES = BN * 4;
 constexpr int P_BYTES = BM * BN;
-constexpr int THREADS = 320;
+constexpr int SOFTMAX_WARPS = 8;  // two per TMEM lane quarter, 64 columns each
+constexpr int CORR_WARPS = 4;
+constexpr int THREADS = 32 * (2 + SOFTMAX_WARPS + CORR_WARPS);
 constexpr int TMEM_COLS = 512;
-constexpr uint32_t COL_S = 0;
-constexpr uint32_t COL_O0 = 128, COL_O1 = 288;  // the two O tiles (144 columns each)
-__device__ __forceinline__ uint32_t col_o(int b) { return b ? COL_O1 : COL_O0; }
+constexpr uint32_t COL_S0 = 0, COL_S1 = 128;  // double-buffered int32 scores
+constexpr uint32_t COL_O = 256;                // fp32 accumulator, 144 columns (128 values + row sum)
+__device__ __forceinline__ uint32_t col_s(int b) { return b ? COL_S1 : COL_S0; }
 constexpr int MMA_K = 32;
 constexpr uint32_t IDESC_QK = idesc_i8(BM, BN);
 constexpr uint32_t IDESC_PV = idesc_f8_e4m3(BM, NV);
@@ -243,18 +249,20 @@ struct Shared {
   uint64_t q_full;
   uint64_t kv_full[ST];
   uint64_t kv_empty[ST];
-  uint64_t s_full;
-  uint64_t s_free;
+  uint64_t s_full[2];
+  uint64_t s_free[2];
   uint64_t p_full[2];
   uint64_t p_free[2];
-  uint64_t o_full[2];
-  uint64_t o_free[2];
+  uint64_t o_full;
+  uint64_t o_ready;
   uint64_t a_full[AR];
   uint64_t a_free[AR];
+  uint64_t x_full[2][4];  // per iteration parity and lane quarter: both halves' partial maxima written
   uint64_t drain;
   uint32_t tmem_base;
   volatile int abort;
   float alpha[AR][BM];
+  float xmax[2][2][BM];   // [iteration parity][column half][row]
 };
 constexpr size_t SMEM_BYTES = 1024 + OFF_SH + sizeof(Shared);
 
@@ -271,7 +279,19 @@ struct Params {
   float attn_scale;
 };
 
-__global__ void __launch_bounds__(384, 1)
+// int32 -> fp32 for |s| < 2^22 without the conversion unit: the bits of s + 1.5 * 2^23 read as a
+// float are exactly 1.5 * 2^23 + s. Exact for every score (|s| <= 128 * 127 * 127 < 2^21).
+__device__ __forceinline__ float i2f_exact(uint32_t s) {
+  return __fsub_rn(__uint_as_float(s + 0x4B400000u), 12582912.0f);
+}
+
+__device__ __forceinline__ uint32_t f32x4_to_e4m3x4(float a, float b, float c, float d) {
+  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+  return lo | (hi << 16);
+}
+
+__global__ void __launch_bounds__(512, 1)
 flash_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
              const __grid_constant__ CUtensorMap tv, const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -296,17 +316,18 @@ flash_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
       mbar_init(&sh.kv_full[s], 1);
       mbar_init(&sh.kv_empty[s], 1);
     }
-    mbar_init(&sh.s_full, 1);
-    mbar_init(&sh.s_free, 4);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&sh.p_full[b], 128);
+      mbar_init(&sh.s_full[b], 1);
+      mbar_init(&sh.s_free[b], SOFTMAX_WARPS);
+      mbar_init(&sh.p_full[b], 32 * SOFTMAX_WARPS);
       mbar_init(&sh.p_free[b], 1);
-      mbar_init(&sh.o_full[b], 1);
-      mbar_init(&sh.o_free[b], 128);
+      for (int q = 0; q < 4; ++q) mbar_init(&sh.x_full[b][q], 64);
     }
+    mbar_init(&sh.o_full, 1);
+    mbar_init(&sh.o_ready, 32 * CORR_WARPS);
     for (int a = 0; a < AR; ++a) {
-      mbar_init(&sh.a_full[a], 128);
-      mbar_init(&sh.a_free[a], 128);
+      mbar_init(&sh.a_full[a], BM);
+      mbar_init(&sh.a_free[a], 32 * CORR_WARPS);
     }
     mbar_init(&sh.drain, 1);
     sh.abort = 0;
@@ -364,31 +385,33 @@ flash_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
       bool issued_any = false;
       bool ok = mbar_wait(&sh.q_full, 0, kErrWaitTimeoutMma) && !sh.abort;
       const uint32_t qa = smem_u32(sQ);
+      // O += P_i V_i, after the correction warps rescaled O by alpha_i (i > 0)
       auto issue_pv = [&](int i) -> bool {
         const int b = i & 1;
         const int s = i % ST;
         if (!mbar_wait(&sh.p_full[b], (i >> 1) & 1, kErrWaitTimeoutMma)) return false;
-        if (!mbar_wait(&sh.o_free[b], ((i >> 1) & 1) ^ 1, kErrWaitTimeoutMma)) return false;
+        if (i > 0 && !mbar_wait(&sh.o_ready, (i - 1) & 1, kErrWaitTimeoutMma)) return false;
         if (sh.abort) return false;
         tc_fence_after();
         const uint32_t pa = smem_u32(sP + b * P_BYTES);
         const uint32_t vb = smem_u32(sV + s * V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BN / MMA_K; ++kk)
-          mma_f8(tmem + col_o(b), smem_desc_sw128(pa + kk * MMA_K), smem_desc_sw128(vb + kk * MMA_K), IDESC_PV,
-                 kk != 0 ? 1u : 0u);
-        mma_commit(&sh.o_full[b]);
+          mma_f8(tmem + COL_O, smem_desc_sw128(pa + kk * MMA_K), smem_desc_sw128(vb + kk * MMA_K), IDESC_PV,
+                 (i > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&sh.o_full);
         mma_commit(&sh.p_free[b]);
         mma_commit(&sh.kv_empty[s]);
         return true;
       };
       for (int j = 0; ok && j < nk; ++j) {
         const int s = j % ST;
+        const int b = j & 1;
         if (!mbar_wait(&sh.kv_full[s], (j / ST) & 1, kErrWaitTimeoutMma)) {
           ok = false;
           break;
         }
-        if (j > 0 && !mbar_wait(&sh.s_free, (j - 1) & 1, kErrWaitTimeoutMma)) {
+        if (j >= 2 && !mbar_wait(&sh.s_free[b], ((j - 2) >> 1) & 1, kErrWaitTimeoutMma)) {
           ok = false;
           break;
         }
@@ -400,10 +423,10 @@ flash_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         const uint32_t kb = smem_u32(sK + s * K_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / MMA_K; ++kk)
-          mma_i8(tmem + COL_S, smem_desc_sw128(qa + kk * MMA_K), smem_desc_sw128(kb + kk * MMA_K), IDESC_QK,
+          mma_i8(tmem + col_s(b), smem_desc_sw128(qa + kk * MMA_K), smem_desc_sw128(kb + kk * MMA_K), IDESC_QK,
                  kk != 0 ? 1u : 0u);
         issued_any = true;
-        mma_commit(&sh.s_full);
+        mma_commit(&sh.s_full[b]);
         if (j > 0 && !issue_pv(j - 1)) {
           ok = false;
           break;
@@ -417,35 +440,35 @@ flash_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
       }
     }
     __syncwarp();
-  } else if (warp < 6) {
-    // ------------------------------------------------------------ softmax
+  } else if (warp < 2 + SOFTMAX_WARPS) {
+    // ------------------------------------------------------------ softmax (64 columns of one row)
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const int64_t qrow = q0 + row;
     // rows past the end get a positive placeholder scale (their output is never stored)
     const float qsv = qrow < p.seq ? __ldg(p.qs_t + head * p.seq_pad + qrow) : 1.0f;
     const float ra = __fmul_rn(__fmul_rn(qsv, p.attn_scale), kLog2e);
-    const uint32_t t_s = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + COL_S;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(half * 64);
     float m = -INFINITY;
     for (int j = 0; j < nk; ++j) {
-      bool ok = mbar_wait(&sh.s_full, j & 1, kErrWaitTimeoutEpilogue);
+      const int b = j & 1;
+      bool ok = mbar_wait(&sh.s_full[b], (j >> 1) & 1, kErrWaitTimeoutEpilogue);
       ok = __all_sync(0xffffffffu, ok) && !sh.abort;
       if (!ok) {
         sh.abort = 1;
         break;
       }
       tc_fence_after();
-      uint32_t sr[128];
-      tmem_ld_32x32b_x32(t_s + 0, *reinterpret_cast<uint32_t(*)[32]>(sr + 0));
-      tmem_ld_32x32b_x32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-      tmem_ld_32x32b_x32(t_s + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
-      tmem_ld_32x32b_x32(t_s + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
+      uint32_t sr[64];
+      tmem_ld_32x32b_x32(t_lane + col_s(b), *reinterpret_cast<uint32_t(*)[32]>(sr + 0));
+      tmem_ld_32x32b_x32(t_lane + col_s(b) + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
       tmem_ld_wait();
-#pragma unroll
-      for (int c = 0; c < 128; c += 32) reg_dep32(*reinterpret_cast<uint32_t(*)[32]>(sr + c));
+      reg_dep32(*reinterpret_cast<uint32_t(*)[32]>(sr + 0));
+      reg_dep32(*reinterpret_cast<uint32_t(*)[32]>(sr + 32));
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sh.s_free);
+      if (lane == 0) mbar_arrive(&sh.s_free[b]);
       const int s = j % ST;
       // the key scales arrived with this stage (the MMA consumed it before committing S)
       ok = mbar_wait(&sh.kv_full[s], (j / ST) & 1, kErrWaitTimeoutEpilogue);
@@ -454,46 +477,56 @@ flash_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         sh.abort = 1;
         break;
       }
-      const float4* ks4 = reinterpret_cast<const float4*>(sKS + s * KS_BYTES);
-      const int64_t left = p.seq - static_cast<int64_t>(j) * BN;
-      const int valid = left < BN ? static_cast<int>(left) : BN;
-      float y[128];
+      const float4* ks4 = reinterpret_cast<const float4*>(sKS + s * KS_BYTES) + half * 16;
+      const int64_t left = p.seq - static_cast<int64_t>(j) * BN - half * 64;
+      const int valid = left < 64 ? static_cast<int>(left) : 64;
+      float y[64];
 #pragma unroll
-      for (int c = 0; c < 128; c += 4) {
+      for (int c = 0; c < 64; c += 4) {
         const float4 k4 = ks4[c / 4];
-        y[c + 0] = __fmul_rn(__int2float_rn(static_cast<int>(sr[c + 0])), k4.x);
-        y[c + 1] = __fmul_rn(__int2float_rn(static_cast<int>(sr[c + 1])), k4.y);
-        y[c + 2] = __fmul_rn(__int2float_rn(static_cast<int>(sr[c + 2])), k4.z);
-        y[c + 3] = __fmul_rn(__int2float_rn(static_cast<int>(sr[c + 3])), k4.w);
+        y[c + 0] = __fmul_rn(i2f_exact(sr[c + 0]), k4.x);
+        y[c + 1] = __fmul_rn(i2f_exact(sr[c + 1]), k4.y);
+        y[c + 2] = __fmul_rn(i2f_exact(sr[c + 2]), k4.z);
+        y[c + 3] = __fmul_rn(i2f_exact(sr[c + 3]), k4.w);
       }
-      if (valid < BN) {
+      if (valid < 64) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) y[c] = c < valid ? y[c] : -INFINITY;
+        for (int c = 0; c < 64; ++c) y[c] = c < valid ? y[c] : -INFINITY;
       }
       float mx[4] = {y[0], y[1], y[2], y[3]};
 #pragma unroll
-      for (int c = 4; c < 128; c += 8) {
+      for (int c = 4; c < 64; c += 8) {
         mx[0] = fmax3(mx[0], y[c + 0], y[c + 4]);
         mx[1] = fmax3(mx[1], y[c + 1], y[c + 5]);
         mx[2] = fmax3(mx[2], y[c + 2], y[c + 6]);
         mx[3] = fmax3(mx[3], y[c + 3], y[c + 7]);
       }
-      const float mrow = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
-      const float m_new = fmaxf(m, __fmul_rn(mrow, ra));
-      const float alpha = ex2_approx(__fsub_rn(m, m_new));
-      m = m_new;
-      // hand alpha to the correction warps
-      const int a = j % AR;
-      ok = mbar_wait(&sh.a_free[a], ((j / AR) & 1) ^ 1, kErrWaitTimeoutEpilogue);
+      const float pm = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
+      // row maximum over both column halves (bounded mbarrier exchange; -inf for a half past the end)
+      sh.xmax[b][half][row] = pm;
+      mbar_arrive(&sh.x_full[b][quarter]);
+      ok = mbar_wait(&sh.x_full[b][quarter], (j >> 1) & 1, kErrWaitTimeoutEpilogue);
       ok = __all_sync(0xffffffffu, ok) && !sh.abort;
       if (!ok) {
         sh.abort = 1;
         break;
       }
-      sh.alpha[a][row] = alpha;
-      mbar_arrive(&sh.a_full[a]);
+      const float mrow = fmaxf(pm, sh.xmax[b][half ^ 1][row]);
+      const float m_new = fmaxf(m, __fmul_rn(mrow, ra));
+      const float alpha = ex2_approx(__fsub_rn(m, m_new));
+      m = m_new;
+      if (half == 0) {  // hand alpha to the correction warps
+        const int a = j % AR;
+        ok = mbar_wait(&sh.a_free[a], ((j / AR) & 1) ^ 1, kErrWaitTimeoutEpilogue);
+        ok = __all_sync(0xffffffffu, ok) && !sh.abort;
+        if (!ok) {
+          sh.abort = 1;
+          break;
+        }
+        sh.alpha[a][row] = alpha;
+        mbar_arrive(&sh.a_full[a]);
+      }
       // P tile: E4M3, K-major with the 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7))
-      const int b = j & 1;
       ok = mbar_wait(&sh.p_free[b], ((j >> 1) & 1) ^ 1, kErrWaitTimeoutEpilogue);
       ok = __all_sync(0xffffffffu, ok) && !sh.abort;
       if (!ok) {
@@ -503,86 +536,107 @@ flash_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
       uint8_t* prow = sP + b * P_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
       const float nm = -m_new;
 #pragma unroll
-      for (int c16 = 0; c16 < 8; ++c16) {
+      for (int c16 = 0; c16 < 4; ++c16) {
         uint32_t w[4];
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           const int c = c16 * 16 + q4 * 4;
-          const float e0 = ex2_approx(__fmaf_rn(y[c + 0], ra, nm));
-          const float e1 = ex2_approx(__fmaf_rn(y[c + 1], ra, nm));
-          const float e2 = ex2_approx(__fmaf_rn(y[c + 2], ra, nm));
-          const float e3 = ex2_approx(__fmaf_rn(y[c + 3], ra, nm));
-          const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(e0, e1), __NV_SATFINITE, __NV_E4M3);
-          const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(e2, e3), __NV_SATFINITE, __NV_E4M3);
-          w[q4] = lo | (hi << 16);
+          w[q4] = f32x4_to_e4m3x4(ex2_approx(__fmaf_rn(y[c + 0], ra, nm)), ex2_approx(__fmaf_rn(y[c + 1], ra, nm)),
+                                  ex2_approx(__fmaf_rn(y[c + 2], ra, nm)), ex2_approx(__fmaf_rn(y[c + 3], ra, nm)));
         }
-        *reinterpret_cast<uint4*>(prow + ((c16 ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        const int chunk = half * 4 + c16;
+        *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       fence_proxy_async_smem();
       mbar_arrive(&sh.p_full[b]);
     }
   } else {
-    // ------------------------------------------------------------ correction + output
+    // ------------------------------------------------------------ O rescale + output
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    float acc[128];
-#pragma unroll
-    for (int c = 0; c < 128; ++c) acc[c] = 0.0f;
-    float l = 0.0f;
+    const uint32_t t_o = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + COL_O;
     bool good = true;
     for (int i = 0; i < nk; ++i) {
-      const int b = i & 1;
       const int a = i % AR;
-      bool ok = mbar_wait(&sh.o_full[b], (i >> 1) & 1, kErrWaitTimeoutEpilogue);
-      ok = ok && mbar_wait(&sh.a_full[a], (i / AR) & 1, kErrWaitTimeoutEpilogue);
+      bool ok = mbar_wait(&sh.a_full[a], (i / AR) & 1, kErrWaitTimeoutEpilogue);
       ok = __all_sync(0xffffffffu, ok) && !sh.abort;
       if (!ok) {
-        sh.abort = 1;
         good = false;
+        sh.abort = 1;
         break;
       }
       const float alpha = sh.alpha[a][row];
       mbar_arrive(&sh.a_free[a]);
-      tc_fence_after();
-      const uint32_t t_o = t_lane + col_o(b);
-      uint32_t r0[16], r1[16];
-      tmem_ld_32x32b_x16(t_o + 0, r0);
-      tmem_ld_wait();
-      reg_dep16(r0);
-#pragma unroll
-      for (int c = 0; c < 128; c += 32) {
-        // one load in flight while the previous chunk is accumulated
-        tmem_ld_32x32b_x16(t_o + c + 16, r1);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) acc[c + e] = __fmaf_rn(acc[c + e], alpha, __uint_as_float(r0[e]));
-        tmem_ld_wait();
-        reg_dep16(r1);
-        tmem_ld_32x32b_x16(t_o + c + 32, r0);  // c + 32 == 128 on the last pass: the row-sum column
-#pragma unroll
-        for (int e = 0; e < 16; ++e) acc[c + 16 + e] = __fmaf_rn(acc[c + 16 + e], alpha, __uint_as_float(r1[e]));
-        tmem_ld_wait();
-        reg_dep16(r0);
+      if (i == 0) continue;  // P_0 V_0 initialises O
+      // O holds P_0 V_0 + ... + P_{i-1} V_{i-1}: wait for the last of them, then O *= alpha_i
+      // (skipped by a warp whose 32 alphas are all exactly 1: the product would not change O)
+      ok = mbar_wait(&sh.o_full, (i - 1) & 1, kErrWaitTimeoutEpilogue);
+      ok = __all_sync(0xffffffffu, ok) && !sh.abort;
+      if (!ok) {
+        good = false;
+        sh.abort = 1;
+        break;
       }
-      l = __fmaf_rn(l, alpha, __uint_as_float(r0[0]));
-      tc_fence_before();
-      mbar_arrive(&sh.o_free[b]);
-    }
-    const int64_t qrow = q0 + row;
-    if (good && !sh.abort && qrow < p.seq) {
-      const float vs = v_scale_of(__ldg(p.v_amax));
-      uint4* dst = reinterpret_cast<uint4*>(p.out + qrow * p.ldo + static_cast<int64_t>(head) * D);
+      tc_fence_after();
+      if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_o + c, r);
+          tmem_ld_wait();
+          reg_dep32(r);
 #pragma unroll
-      for (int c = 0; c < 128; c += 8) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float lo = __fdiv_rn(__fmul_rn(acc[c + 2 * e], vs), l);
-          const float hi = __fdiv_rn(__fmul_rn(acc[c + 2 * e + 1], vs), l);
-          const __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
-          w[e] = *reinterpret_cast<const uint32_t*>(&h2);
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__fmul_rn(__uint_as_float(r[e]), alpha));
+          tmem_st_32x32b_x32(t_o + c, r);
         }
-        dst[c / 8] = make_uint4(w[0], w[1], w[2], w[3]);
+        uint32_t r16[16];
+        tmem_ld_32x32b_x16(t_o + 128, r16);
+        tmem_ld_wait();
+        reg_dep16(r16);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) r16[e] = __float_as_uint(__fmul_rn(__uint_as_float(r16[e]), alpha));
+        tmem_st_32x32b_x16(t_o + 128, r16);
+        tmem_st_wait();
+      }
+      tc_fence_before();
+      mbar_arrive(&sh.o_ready);
+    }
+    if (good && nk > 0) {
+      bool ok = mbar_wait(&sh.o_full, (nk - 1) & 1, kErrWaitTimeoutEpilogue);
+      ok = __all_sync(0xffffffffu, ok) && !sh.abort;
+      if (ok) {
+        tc_fence_after();
+        uint32_t r16[16];
+        tmem_ld_32x32b_x16(t_o + 128, r16);
+        tmem_ld_wait();
+        reg_dep16(r16);
+        const float l = __uint_as_float(r16[0]);
+        const int64_t qrow = q0 + row;
+        const float vs = v_scale_of(__ldg(p.v_amax));
+        uint4* dst = reinterpret_cast<uint4*>(p.out + qrow * p.ldo + static_cast<int64_t>(head) * D);
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_o + c, r);
+          tmem_ld_wait();
+          reg_dep32(r);
+          if (qrow < p.seq) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float lo = __fdiv_rn(__fmul_rn(__uint_as_float(r[8 * v + 2 * e]), vs), l);
+                const float hi = __fdiv_rn(__fmul_rn(__uint_as_float(r[8 * v + 2 * e + 1]), vs), l);
+                const __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
+                w[e] = *reinterpret_cast<const uint32_t*>(&h2);
+              }
+              dst[c / 8 + v] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+      } else {
+        sh.abort = 1;
       }
     }
   }
@@ -648,15 +702,22 @@ cudaError_t launch_attn_quant_qk(const void* src, int64_t seq, int64_t seq_pad, 
   return cudaGetLastError();
 }
 
-cudaError_t launch_attn_quant_v(const void* src, int64_t seq, int64_t seq_pad, int heads, int64_t row_stride,
-                                int64_t v_off, uint8_t* v_t, float* v_amax, cudaStream_t st) {
+cudaError_t launch_attn_v_amax(const void* src, int64_t seq, int heads, int64_t row_stride, int64_t v_off,
+                               float* v_amax, cudaStream_t st) {
   cudaError_t e = cudaMemsetAsync(v_amax, 0, sizeof(float), st);
   if (e != cudaSuccess) return e;
   const int grid_a = sm_count() * 8;
   attn::v_amax_kernel<<<grid_a, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), seq, heads, row_stride, v_off,
                                                v_amax);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attn_quant_v(const void* src, int64_t seq, int64_t seq_pad, int heads, int64_t row_stride,
+                                int64_t v_off, uint8_t* v_t, float* v_amax, bool amax_given, cudaStream_t st) {
+  if (!amax_given) {
+    cudaError_t e = launch_attn_v_amax(src, seq, heads, row_stride, v_off, v_amax, st);
+    if (e != cudaSuccess) return e;
+  }
   attn::quant_v_kernel<<<dim3(static_cast<unsigned>(seq_pad / 128), static_cast<unsigned>(heads)), 256, 0, st>>>(
       static_cast<const __nv_bfloat16*>(src), seq, seq_pad, heads, row_stride, v_off, v_amax, v_t);
   return cudaGetLastError();
@@ -770,6 +831,46 @@ int slim_attn_quant_qk(const void* qkv, int64_t seq, int heads, int dim, int64_t
   return SLIM_OK;
 }
 
+static int attn_v_checks(const void* qkv, int64_t seq, int heads, int dim, int64_t row_stride, int64_t v_offset,
+                         const float* v_amax) {
+  int rc;
+  if ((rc = attn_shape_checks(seq, heads, dim)) != SLIM_OK) return rc;
+  if (seq == 0) return SLIM_OK;
+  if (qkv == nullptr || v_amax == nullptr) return fail(SLIM_ERR_NULL, "qkv/v_amax is NULL");
+  if (row_stride < static_cast<int64_t>(heads) * dim || v_offset < 0) return fail(SLIM_ERR_SHAPE, "bad row stride / offset");
+  if (!aligned16(qkv) || (row_stride % 8) || (v_offset % 8) || (reinterpret_cast<uintptr_t>(v_amax) & 3u))
+    return fail(SLIM_ERR_ALIGN, "qkv rows and offset must be 16-byte aligned");
+  return SLIM_OK;
+}
+
+int slim_attn_v_amax(const void* qkv, int64_t seq, int heads, int dim, int64_t row_stride, int64_t v_offset,
+                     float* v_amax, void* stream) {
+  int rc;
+  if ((rc = attn_v_checks(qkv, seq, heads, dim, row_stride, v_offset, v_amax)) != SLIM_OK) return rc;
+  if (seq == 0) return SLIM_OK;
+  if ((rc = check_arch()) != SLIM_OK) return rc;
+  cudaError_t e = launch_attn_v_amax(qkv, seq, heads, row_stride, v_offset, v_amax, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attention v amax launch");
+  note_launch();
+  return SLIM_OK;
+}
+
+int slim_attn_quant_v_scaled(const void* qkv, int64_t seq, int heads, int dim, int64_t row_stride, int64_t v_offset,
+                             uint8_t* v_t, int64_t seq_pad, const float* v_amax, void* stream) {
+  int rc;
+  if ((rc = attn_v_checks(qkv, seq, heads, dim, row_stride, v_offset, v_amax)) != SLIM_OK) return rc;
+  if ((rc = seq_pad_check(seq, seq_pad)) != SLIM_OK) return rc;
+  if (seq == 0) return SLIM_OK;
+  if (v_t == nullptr) return fail(SLIM_ERR_NULL, "v_t is NULL");
+  if (!aligned16(v_t)) return fail(SLIM_ERR_ALIGN, "v_t must be 16-byte aligned");
+  if ((rc = check_arch()) != SLIM_OK) return rc;
+  cudaError_t e = launch_attn_quant_v(qkv, seq, seq_pad, heads, row_stride, v_offset, v_t, const_cast<float*>(v_amax),
+                                      true, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attention v quantiser launch");
+  note_launch();
+  return SLIM_OK;
+}
+
 int slim_attn_quant_v(const void* qkv, int64_t seq, int heads, int dim, int64_t row_stride, int64_t v_offset,
                       uint8_t* v_t, int64_t seq_pad, float* v_amax, void* stream) {
   int rc;
@@ -782,7 +883,7 @@ int slim_attn_quant_v(const void* qkv, int64_t seq, int heads, int dim, int64_t 
       (reinterpret_cast<uintptr_t>(v_amax) & 3u))
     return fail(SLIM_ERR_ALIGN, "qkv rows, offset and v_t must be 16-byte aligned");
   if ((rc = check_arch()) != SLIM_OK) return rc;
-  cudaError_t e = launch_attn_quant_v(qkv, seq, seq_pad, heads, row_stride, v_offset, v_t, v_amax,
+  cudaError_t e = launch_attn_quant_v(qkv, seq, seq_pad, heads, row_stride, v_offset, v_t, v_amax, false,
                                       static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attention v quantiser launch");
   note_launch(2);

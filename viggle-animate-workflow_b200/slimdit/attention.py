@@ -23,11 +23,11 @@ import ctypes
 import time
 
 DEFAULT_MIN_SEQ = 12000  # below this the dense path wins outright (attention_triton.py:34)
-# The sm_100a kernel has one geometry: 128 query rows x 128 keys per step, 10 warps, a 3-deep
+# The sm_100a kernel has one geometry: 128 query rows x 128 keys per step, 14 warps, a 3-deep
 # K/V ring. The fields are kept so callers that set them still work; the kernel ignores them.
 DEFAULT_BLOCK_M = 128
 DEFAULT_BLOCK_N = 128
-DEFAULT_WARPS = 10
+DEFAULT_WARPS = 14
 DEFAULT_STAGES = 3
 QUANT_BLOCK = 64
 HEAD_DIM = 128  # the one head dim the kernel supports (MiniMax-H3: 56 heads x 128)
@@ -190,6 +190,53 @@ def attention_quantized(ops: dict, seq: int, heads: int, scale: float, out=None)
     return out
 
 
+def attention_heads(qkv, heads: int, rank: int, world: int, rotate: bool = True, group=None, out=None):
+    """Heads [rank*H/world, (rank+1)*H/world) of the packed [seq, 3*H*128] buffer on this GPU ->
+    bf16 [seq, H/world*128].
+
+    The V scale is one number for the whole tensor (attention_triton.py:283-286): every rank
+    computes max|v| over its own heads, the maxima are all-reduced (MAX, one float), and every
+    rank quantises with the global value, so the result equals the single-GPU one bit for bit.
+    Q/K quantisation and the attention itself are per head; no other data crosses GPUs."""
+    from . import _native as nat
+    import torch.distributed as dist
+
+    torch = nat.require_cuda()
+    if heads % world:
+        raise ValueError(f"{heads} heads do not split over {world} ranks")
+    hl = heads // world
+    h0 = rank * hl
+    hd = heads * HEAD_DIM
+    seq = qkv.shape[0]
+    if qkv.shape[1] != 3 * hd or qkv.stride(1) != 1 or qkv.dtype != torch.bfloat16:
+        raise ValueError("qkv must be a bf16 [seq, 3*heads*128] tensor with unit column stride")
+    seq_pad = (seq + 127) // 128 * 128
+    dev = qkv.device
+    lib = nat.load()
+    st = torch.cuda.current_stream(dev).cuda_stream
+    q = torch.empty((seq, hl * HEAD_DIM), dtype=torch.int8, device=dev)
+    k = torch.empty_like(q)
+    qs = torch.empty((hl, seq_pad), dtype=torch.float32, device=dev)
+    ks = torch.empty_like(qs)
+    v = torch.empty((hl, HEAD_DIM, seq_pad), dtype=torch.uint8, device=dev)
+    amax = torch.empty((1,), dtype=torch.float32, device=dev)
+    if out is None:
+        out = torch.empty((seq, hl * HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    row = qkv.stride(0)
+    nat.check(lib.slim_attn_quant_qk(qkv.data_ptr(), seq, hl, HEAD_DIM, row, h0 * HEAD_DIM, hd + h0 * HEAD_DIM,
+                                     int(bool(rotate)), q.data_ptr(), qs.data_ptr(), k.data_ptr(), ks.data_ptr(),
+                                     seq_pad, st))
+    nat.check(lib.slim_attn_v_amax(qkv.data_ptr(), seq, hl, HEAD_DIM, row, 2 * hd + h0 * HEAD_DIM, amax.data_ptr(), st))
+    if world > 1:
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=group)
+    nat.check(lib.slim_attn_quant_v_scaled(qkv.data_ptr(), seq, hl, HEAD_DIM, row, 2 * hd + h0 * HEAD_DIM,
+                                           v.data_ptr(), seq_pad, amax.data_ptr(), st))
+    nat.check(lib.slim_attn_int8(q.data_ptr(), qs.data_ptr(), k.data_ptr(), ks.data_ptr(), v.data_ptr(),
+                                 amax.data_ptr(), attn_scale(HEAD_DIM, rotate), seq, hl, HEAD_DIM, seq_pad,
+                                 out.data_ptr(), out.stride(0), st))
+    return out
+
+
 class TritonAttnConfig:
     """Knobs of the override (attention_triton.py:225-245). ``block_m``/``block_n``/``num_warps``/
     ``num_stages`` are accepted for compatibility; the sm_100a kernel has one fixed geometry."""
@@ -304,6 +351,7 @@ def install_triton_attn(config=None, stats=None):
 
 
 __all__ = [
-    "DEFAULT_MIN_SEQ", "HEAD_DIM", "TritonAttnConfig", "TritonAttnOverride", "attention_packed", "attention_quantized",
+    "DEFAULT_MIN_SEQ", "HEAD_DIM", "TritonAttnConfig", "TritonAttnOverride", "attention_heads", "attention_packed",
+    "attention_quantized",
     "attn_scale", "install_triton_attn", "packed_geometry", "quantized_operands", "unwrap", "workspace_bytes",
 ]
