@@ -59,6 +59,8 @@ def parse_args(argv=None):
                     help="run only a small case of one workload (for ncu captures; prints no bench line)")
     ap.add_argument("--tokens", type=int, default=16384, help="token rows of the --profile-case run")
     ap.add_argument("--heads", type=int, default=4, help="attention heads of the --profile-case attn run")
+    ap.add_argument("--convert-blocks", type=int, default=4,
+                    help="MiniMax-H3 blocks in the end-to-end converter line (0 skips it)")
     return ap.parse_args(argv)
 
 
@@ -324,6 +326,70 @@ def run_attention(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
         res["tensor_frac_of_int8_peak"] = round(total_ops / (flash_ms * 1e-3) / 1e12 / peak, 3)
         res["peak_tops"] = round(peak, 1)
     return res
+
+
+# ----------------------------------------------------------------------------- converter end to end
+def run_convert_e2e(torch, dev, blocks: int) -> dict:
+    """The whole converter on real-shape shards: `blocks` MiniMax-H3 blocks (hidden 5120, FFN
+    13824) plus the global tensors as bf16 safetensors in a temporary directory (random
+    N(0, 0.02) weights drawn on the GPU), converted twice: ops one at a time, then pipelined
+    (reads, GPU work and writes overlapped); the two files must be byte-identical."""
+    import contextlib
+    import hashlib
+    import shutil
+
+    import numpy as np
+
+    import synthetic
+    from slimdit.convert import convert
+
+    work = Path(tempfile.mkdtemp(prefix="slim_convert_e2e_"))
+    try:
+        src = work / "official"
+        src.mkdir()
+        shapes = synthetic.official_shapes(blocks, 5120, 13824, 256)
+        g = torch.Generator(device=dev)
+        g.manual_seed(3)
+        names = sorted(shapes)
+        per = (len(names) + 1) // 2
+        src_bytes = 0
+        for s_i in range(2):
+            part = {}
+            for name in names[s_i * per:(s_i + 1) * per]:
+                if name == "rope.inv_freq":
+                    part[name] = (1.0 / (10000.0 ** (np.arange(16, dtype=np.float32) / 16))).astype(np.float32)
+                else:
+                    t = (torch.randn(shapes[name], generator=g, device=dev) * 0.02).to(torch.bfloat16)
+                    part[name] = t.view(torch.int16).cpu().numpy().view(np.uint16)
+                src_bytes += part[name].nbytes
+            synthetic._write_safetensors(src / f"diffusion_pytorch_model-{s_i + 1:05d}-of-00002.safetensors", part)
+            del part
+        res = {"workload": f"{blocks} MiniMax-H3 blocks (hidden 5120, FFN 13824) + global tensors: bf16 shards -> "
+                           f"adaLN curve + INT8 convrot file, rank 8, grid 1025, error report on",
+               "source_gb": round(src_bytes / 1e9, 3), "unit": "GB/s", "source": "page-cache resident shards"}
+        digests = {}
+        # each mode twice: the first run in a process pays pinned allocations and library set-up
+        for mode in ("sequential", "pipelined"):
+            for attempt in ("cold", "warm"):
+                out = work / f"{mode}.safetensors"
+                with contextlib.redirect_stdout(sys.stderr):
+                    t0 = time.perf_counter()
+                    convert(src, out, rank=8, grid=1025, pipeline=(mode == "pipelined"))
+                    dt = time.perf_counter() - t0
+                res[f"{mode}_s" if attempt == "warm" else f"{mode}_cold_s"] = round(dt, 3)
+                h = hashlib.sha256()
+                with out.open("rb") as fh:
+                    for chunk in iter(lambda: fh.read(1 << 24), b""):
+                        h.update(chunk)
+                digests[f"{mode}/{attempt}"] = h.hexdigest()
+                res["output_gb"] = round(out.stat().st_size / 1e9, 3)
+                out.unlink()
+        res["identical"] = len(set(digests.values())) == 1
+        res["value"] = round(src_bytes / 1e9 / res["pipelined_s"], 3)
+        res["sequential_gbs"] = round(src_bytes / 1e9 / res["sequential_s"], 3)
+        return res
+    finally:
+        shutil.rmtree(work, ignore_errors=True)
 
 
 # ----------------------------------------------------------------------------- secondary workloads
@@ -790,6 +856,8 @@ def run_ours(args) -> int:
     secondary = None
     if not args.no_secondary:
         secondary = run_secondary(torch, dev, lib, world, rank, args.secondary_steps, barrier, reduce_max)
+        if world == 1 and args.convert_blocks > 0:
+            secondary["convert_e2e"] = run_convert_e2e(torch, dev, args.convert_blocks)
 
     # max over ranks
     vals = torch.tensor([total_ms, gemm_ms, quant_ms, e2e["ms"] if e2e else 0.0], device=dev, dtype=torch.float64)

@@ -202,3 +202,29 @@ def test_multi_process_split_writes_the_same_bytes(official_dir, golden_meta, tm
                        nprocs=world, join=True, start_method="spawn")
     assert all((tmp_path / f"ok{r}").exists() for r in range(world))
     assert hashlib.sha256(out.read_bytes()).hexdigest() == golden_meta["convert_block0"]["sha256_file"]
+
+
+def test_byte_level_copies_equal_the_torch_path(tmp_path):
+    """Copy/concat ops assembled from the stored bytes (positional reads, half swaps, exact
+    bf16 -> f32 widening) give the bytes of the torch cast path the reference uses."""
+    import torch
+
+    import synthetic
+    from slimdit import mapping
+    from slimdit.convert import _prepare, _raw_bytes
+    from slimdit.safetensors_io import ShardSet, to_bytes
+
+    src = ShardSet(synthetic.official_checkpoint(tmp_path / "official", n_blocks=2))
+    checked = 0
+    for op in mapping.build_plan(src.manifest.keys()):
+        if op.kind not in ("copy", "concat"):
+            continue
+        raw = _raw_bytes(src, op)
+        if raw is None:
+            continue
+        parts = [src.get(s) for s in op.src]
+        merged = parts[0] if len(parts) == 1 else torch.cat(parts, dim=0)
+        assert bytes(memoryview(raw).cast("B")) == to_bytes(_prepare(merged, op), op.dtype.upper()), op.out
+        checked += 1
+    src.close()
+    assert checked >= 20

@@ -178,14 +178,200 @@ class _GpuQuantizer:
         return q_h.numpy(), s_h.numpy(), err
 
 
+_ST_TORCH = {"BF16": torch.bfloat16, "F16": torch.float16, "F32": torch.float32}
+
+
+def _raw_bytes(src: ShardSet, op: mapping.Op) -> np.ndarray | None:
+    """The output bytes of a copy/concat op assembled from the sources' stored bytes, when the
+    op is a pure byte rearrangement (same dtype, optional half swap) or a bf16 -> f32 widening
+    (exact); None when it needs a rounding cast (done with torch as in the reference)."""
+    dts = {src.manifest[name][0] for name in op.src}
+    target = op.dtype.upper()
+    if len(dts) != 1:
+        return None
+    stored = dts.pop()
+    if stored != target and not (stored == "BF16" and target == "F32"):
+        return None
+    total = sum(src.nbytes(name) for name in op.src)
+    buf = np.empty((total,), dtype=np.uint8)
+    off = 0
+    for name in op.src:
+        off += src.read_into(name, buf, off)
+    if op.swap_halves:
+        rows = sum(src.manifest[name][1][0] for name in op.src)
+        if rows % 2:
+            raise ValueError(f"{op.out[0]}: cannot swap halves of {rows} rows")
+        half = total // 2
+        buf = np.concatenate([buf[half:], buf[:half]])
+    if stored == target:
+        return buf
+    return (buf.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+class _HostWiden:
+    """bf16 -> fp32 of a large source tensor (exact, as the reference's ``.float()``) from its
+    stored bytes, into buffers reused per host thread (no per-call allocation)."""
+
+    def __init__(self):
+        import threading
+
+        self.local = threading.local()
+
+    @staticmethod
+    def accepts(src: ShardSet, name: str) -> bool:
+        return src.manifest[name][0] == "BF16" and len(src.manifest[name][1]) == 2
+
+    def __call__(self, src: ShardSet, name: str) -> np.ndarray:
+        rows, cols = src.manifest[name][1]
+        n = rows * cols
+        loc = self.local
+        if getattr(loc, "u16", None) is None or loc.u16.size < n:
+            loc.u16 = np.empty((n,), dtype=np.uint16)
+            loc.u32 = np.empty((n,), dtype=np.uint32)
+        u16, u32 = loc.u16[:n], loc.u32[:n]
+        src.read_into(name, u16.view(np.uint8), 0)
+        np.left_shift(u16, 16, out=u32, dtype=np.uint32)
+        return u32.view(np.float32).reshape(rows, cols)
+
+
+class _Pipeline:
+    """The quantised linears of one process as a three-stage pipeline, so that reading the
+    sources, the GPU work and writing the results overlap across linears instead of taking
+    turns:
+
+    * reader threads (two): the source tensors' stored bytes straight from the shard files into
+      pinned staging buffers (positional reads, concatenated in q/k/v order);
+    * this thread: one async H2D per linear on a copy stream, then on a compute stream the
+      half swap, the reference-order rotate + INT8 kernel, the device error report and the
+      D2H of codes and scales into pinned output buffers;
+    * writer thread: waits for that linear's D2H event and writes its three tensors at their
+      header offsets.
+
+    DEPTH staging buffers of each kind rotate; a buffer is refilled only after the copy that
+    read it (CUDA event) or the write that used it (future) has finished. The bytes written
+    are those of the sequential path: same kernel, same inputs, positional writes."""
+
+    DEPTH = 3
+
+    def __init__(self, device: torch.device, src: ShardSet, writer, blob: bytes, with_error: bool):
+        from concurrent.futures import ThreadPoolExecutor
+
+        from . import ops
+
+        self.ops = ops
+        self.dev = device
+        self.src = src
+        self.writer = writer
+        self.blob = blob
+        self.with_error = with_error
+        self.h2d = torch.cuda.Stream(device)
+        self.comp = torch.cuda.Stream(device)
+        self.reader = ThreadPoolExecutor(2, thread_name_prefix="convert-read")
+        self.wpool = ThreadPoolExecutor(1, thread_name_prefix="convert-write")
+        self.stage_in: list = [None] * self.DEPTH
+        self.stage_q: list = [None] * self.DEPTH
+        self.stage_s: list = [None] * self.DEPTH
+        self.in_done: list = [None] * self.DEPTH     # event: the H2D that read stage_in[slot]
+        self.out_done: list = [None] * self.DEPTH    # future: the write that used stage_q/s[slot]
+        self.errors: list = []
+
+    @staticmethod
+    def accepts(op, src: ShardSet) -> bool:
+        return all(src.manifest[name][0] in _ST_TORCH for name in op.src) and \
+            len({src.manifest[name][0] for name in op.src}) == 1
+
+    def _pinned(self, store: list, slot: int, nbytes: int) -> torch.Tensor:
+        buf = store[slot]
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty((nbytes,), dtype=torch.uint8, pin_memory=True)
+            store[slot] = buf
+        return buf
+
+    def _read(self, op, slot: int):
+        if self.in_done[slot] is not None:
+            self.in_done[slot].synchronize()
+        nbytes = sum(self.src.nbytes(name) for name in op.src)
+        buf = self._pinned(self.stage_in, slot, nbytes)
+        arr = buf.numpy()
+        off = 0
+        for name in op.src:
+            off += self.src.read_into(name, arr, off)
+        rows = sum(self.src.manifest[name][1][0] for name in op.src)
+        cols = self.src.manifest[op.src[0]][1][1]
+        return buf, nbytes, _ST_TORCH[self.src.manifest[op.src[0]][0]], rows, cols
+
+    def _write(self, base: str, done: torch.cuda.Event, q_buf, s_buf, nq: int, ns: int, keep) -> None:
+        done.synchronize()
+        del keep
+        self.writer.write(f"{base}.weight", memoryview(q_buf.numpy()[:nq]))
+        self.writer.write(f"{base}.weight_scale", memoryview(s_buf.numpy()[:ns]))
+        self.writer.write(f"{base}.comfy_quant", self.blob)
+
+    def run(self, quant_ops: list) -> list[float]:
+        from collections import deque
+
+        reads: deque = deque()
+        nxt = 0
+        for i, op in enumerate(quant_ops):
+            while nxt < len(quant_ops) and len(reads) < self.DEPTH - 1:
+                reads.append(self.reader.submit(self._read, quant_ops[nxt], nxt % self.DEPTH))
+                nxt += 1
+            buf, nbytes, dtype, rows, cols = reads.popleft().result()
+            slot = i % self.DEPTH
+            with torch.cuda.device(self.dev):
+                with torch.cuda.stream(self.h2d):
+                    raw = torch.empty((nbytes,), dtype=torch.uint8, device=self.dev)
+                    raw.copy_(buf[:nbytes], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(self.h2d)
+                self.in_done[slot] = ev
+                if self.out_done[slot] is not None:
+                    self.out_done[slot].result()  # the output staging of this slot is written out
+                with torch.cuda.stream(self.comp):
+                    self.comp.wait_event(ev)
+                    raw.record_stream(self.comp)
+                    w = raw.view(dtype).view(rows, cols)
+                    if op.swap_halves:
+                        half = rows // 2
+                        if half * 2 != rows:
+                            raise ValueError(f"cannot swap halves of {rows} rows")
+                        w = torch.cat([w[half:], w[:half]], dim=0)
+                    q, scale = self.ops.rotate_quant(w, 256, order="reference")
+                    if self.with_error:
+                        deq = self.ops.dequantize(q, scale)
+                        wf = w.float()
+                        self.errors.append(torch.linalg.vector_norm(deq - wf) / torch.linalg.vector_norm(wf))
+                        del deq, wf
+                    nq, ns = q.numel(), scale.numel() * 4
+                    q_buf = self._pinned(self.stage_q, slot, nq)
+                    s_buf = self._pinned(self.stage_s, slot, ns)
+                    q_buf[:nq].copy_(q.view(-1).view(torch.uint8), non_blocking=True)
+                    s_buf[:ns].copy_(scale.view(-1).view(torch.uint8), non_blocking=True)
+                    done = torch.cuda.Event()
+                    done.record(self.comp)
+            base = op.out[0][: -len(".weight")]
+            self.out_done[slot] = self.wpool.submit(self._write, base, done, q_buf, s_buf, nq, ns, (raw, w, q, scale))
+        for f in self.out_done:
+            if f is not None:
+                f.result()
+        self.reader.shutdown()
+        self.wpool.shutdown()
+        torch.cuda.synchronize(self.dev)
+        return [float(e) for e in self.errors]
+
+
 def convert(src_dir: str | Path, out_path: str | Path, rank: int = 8, grid: int = 1025, block_limit: int | None = None,
             verify_blocks: int = 0, curve_dtype: str = "f16", metadata: dict | None = None,
-            quant: str = "int8_convrot", quant_report: bool = True) -> Report:
+            quant: str = "int8_convrot", quant_report: bool = True, pipeline: bool = True) -> Report:
     """Write the converted checkpoint; returns the quantisation/curve report.
 
     Same arguments as the reference's ``convert``; ``quant_report=False`` skips the
     dequantise-and-compare error report. Under ``torch.distributed`` each process converts
-    its share of the tensors on its current CUDA device.
+    its share of the tensors on its current CUDA device. ``pipeline=True`` overlaps source
+    reads, GPU work and writes across the INT8 linears (``_Pipeline``) and runs the curve
+    basis and the curve, copy and derived tensors on four host threads alongside (copies as
+    positional byte moves, the adaLN weights widened from their stored bf16 bytes);
+    ``pipeline=False`` takes the ops one at a time. Both write the same bytes.
     """
     worker, workers = _dist()
     src = ShardSet(src_dir)
@@ -206,14 +392,15 @@ def convert(src_dir: str | Path, out_path: str | Path, rank: int = 8, grid: int 
     if worker != 0:
         writer = OffsetWriter(out_path, manifest, metadata or {"format": "pt"}, create=False)
 
-    table = basis = None
     need_basis = worker == 0 or any(op.kind == "curve" for op in mine) or verify_blocks
-    if need_basis:
-        table, basis, _curve = curve_mod.build_curve_basis(
+
+    def build_basis():
+        table_, basis_, _curve = curve_mod.build_curve_basis(
             *(src.get(name).float().numpy() for name in mapping.CURVE_SOURCES), rank=rank, grid=grid)
         del _curve
-    if worker == 0:
-        writer.write("adaln_t_table", to_bytes(torch.from_numpy(table), "F32"))
+        if worker == 0:
+            writer.write("adaln_t_table", to_bytes(torch.from_numpy(table_), "F32"))
+        return table_, basis_
 
     quantizer = None
     if any(op.kind == "quant" for op in mine):
@@ -224,8 +411,56 @@ def convert(src_dir: str | Path, out_path: str | Path, rank: int = 8, grid: int 
             quantizer = _GpuQuantizer(torch.device("cuda", torch.cuda.current_device()))
     blob = comfy_quant_blob().tobytes()
 
+    piped: list = []
+    host_jobs = None
+    basis_job = None
+    if pipeline and quant == "int8_convrot" and quantizer is not None:
+        piped = [op for op in mine if op.kind == "quant" and _Pipeline.accepts(op, src)]
+    if pipeline:
+        from concurrent.futures import ThreadPoolExecutor
+        host_jobs = ThreadPoolExecutor(4, thread_name_prefix="convert-host")
+        if need_basis:
+            basis_job = host_jobs.submit(build_basis)
+    elif need_basis:
+        table, basis = build_basis()
+    host_futs = []
+    piped_ids = {id(op) for op in piped}
+    widen = _HostWiden() if pipeline else None
+
+    def host_op(op):
+        name = op.out[0]
+        raw = _raw_bytes(src, op) if op.kind in ("copy", "concat") else None
+        if raw is not None:
+            writer.write(name, raw)
+        elif op.kind == "copy":
+            writer.write(name, to_bytes(_prepare(src.get(op.src[0]), op), op.dtype.upper()))
+        elif op.kind == "concat":
+            parts = [src.get(s) for s in op.src]
+            merged = parts[0] if len(parts) == 1 else torch.cat(parts, dim=0)
+            writer.write(name, to_bytes(_prepare(merged, op), op.dtype.upper()))
+        elif op.kind == "curve":
+            # widen first: only the projection needs the basis (still being built on another thread)
+            weight = widen(src, op.src[0]) if widen is not None and widen.accepts(src, op.src[0]) else \
+                src.get(op.src[0]).float().numpy()
+            basis_ = basis_job.result()[1] if basis_job is not None else basis
+            projected = curve_mod.project_weight(weight, basis_)
+            writer.write(name, to_bytes(torch.from_numpy(projected), curve_dtype.upper()))
+        elif op.kind == "derived":
+            from .rope import rope_inv_freq
+            writer.write(name, rope_inv_freq().tobytes())
+        else:
+            raise ValueError(f"unhandled op kind {op.kind!r}")
+
+    if host_jobs is not None:
+        host_futs = [host_jobs.submit(host_op, op) for op in mine if op.kind != "quant"]
+    errors_by_op: dict[int, float] = {}
+    if piped:
+        piped_errors = _Pipeline(quantizer.device, src, writer, blob, quant_report).run(piped)
+        errors_by_op.update((id(op), e) for op, e in zip(piped, piped_errors))
     for op in tqdm(mine, unit="op", desc=f"convert[{worker}/{workers}]", disable=workers > 1 and worker != 0):
         name = op.out[0]
+        if id(op) in piped_ids or (host_jobs is not None and op.kind != "quant"):
+            continue
         if op.kind == "quant":
             base = name[: -len(".weight")]
             parts = [src.get(s) for s in op.src]
@@ -242,25 +477,21 @@ def convert(src_dir: str | Path, out_path: str | Path, rank: int = 8, grid: int 
                 writer.write(f"{base}.weight_scale_2", np.float32(ts).tobytes())
                 writer.write(f"{base}.comfy_quant", nvfp4.comfy_quant_blob().tobytes())
             if err is not None:
-                report.quant_errors.append(err)
+                errors_by_op[id(op)] = err
             del parts
-        elif op.kind == "copy":
-            writer.write(name, to_bytes(_prepare(src.get(op.src[0]), op), op.dtype.upper()))
-        elif op.kind == "concat":
-            parts = [src.get(s) for s in op.src]
-            merged = parts[0] if len(parts) == 1 else torch.cat(parts, dim=0)
-            writer.write(name, to_bytes(_prepare(merged, op), op.dtype.upper()))
-        elif op.kind == "curve":
-            projected = curve_mod.project_weight(src.get(op.src[0]).float().numpy(), basis)
-            writer.write(name, to_bytes(torch.from_numpy(projected), curve_dtype.upper()))
-        elif op.kind == "derived":
-            from .rope import rope_inv_freq
-            writer.write(name, rope_inv_freq().tobytes())
         else:
-            raise ValueError(f"unhandled op kind {op.kind!r}")
+            host_op(op)
 
+    for f in host_futs:
+        f.result()
+    if basis_job is not None:
+        table, basis = basis_job.result()
+    if host_jobs is not None:
+        host_jobs.shutdown()
+    report.quant_errors = [errors_by_op[id(op)] for op in mine if id(op) in errors_by_op]
     expect = {n for op in mine for n in _outputs(op, quant)} | ({"adaln_t_table"} if worker == 0 else set())
     writer.close(expect=expect)
+    src.close()
     _barrier(workers)
     if workers > 1:
         gathered: list = [None] * workers
