@@ -376,6 +376,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Hardware reciprocal (PTX rcp.approx.ftz.f32; +inf -> +0).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // max(a, b, c) in one instruction (sm_100).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float y;
