@@ -19,7 +19,8 @@
 //   flash_kernel      one CTA per (128-query tile, head), 14 warps (flash_int8, :131-174):
 //     warp 0       TMA producer: Q tile once; per key tile the K tile (128 keys x 128 B), the
 //                  V^T tile (128 value columns x 128 keys) and 128 key scales (bulk copy) into
-//                  a 3-stage ring.
+//                  a 4-stage ring (a stage frees only after its PV product; under load a TMA
+//                  round trip is ~2 us, so three stages left the QK products waiting).
 //     warp 1       TMEM (S int32 double-buffered at columns 0 and 128, O fp32 at 256) and one
 //                  lane issuing the MMAs: S_j = Q K_j^T (kind::i8, M=N=128) and O += P_j V_j
 //                  (kind::f8f6f4 E4M3, M=128, N=144). V's smem tile carries 16 extra rows, the
@@ -219,7 +220,7 @@ namespace fl {
 constexpr int BM = 128;           // query rows per CTA
 constexpr int BN = 128;           // keys per tile
 constexpr int NV = 144;           // PV MMA N: 128 value columns + 16 rows (the first all ones)
-constexpr int ST = 3;             // K/V ring depth
+constexpr int ST = 4;             // K/V ring depth
 constexpr int AR = 4;             // alpha ring depth
 constexpr int Q_BYTES = BM * D;
 constexpr int K_BYTES = BN * D;

@@ -23,12 +23,12 @@ import ctypes
 import time
 
 DEFAULT_MIN_SEQ = 12000  # below this the dense path wins outright (attention_triton.py:34)
-# The sm_100a kernel has one geometry: 128 query rows x 128 keys per step, 14 warps, a 3-deep
+# The sm_100a kernel has one geometry: 128 query rows x 128 keys per step, 14 warps, a 4-deep
 # K/V ring. The fields are kept so callers that set them still work; the kernel ignores them.
 DEFAULT_BLOCK_M = 128
 DEFAULT_BLOCK_N = 128
 DEFAULT_WARPS = 14
-DEFAULT_STAGES = 3
+DEFAULT_STAGES = 4
 QUANT_BLOCK = 64
 HEAD_DIM = 128  # the one head dim the kernel supports (MiniMax-H3: 56 heads x 128)
 
