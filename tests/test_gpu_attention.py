@@ -85,7 +85,7 @@ def test_quantisers_bit_exact(cuda, seq, heads, rotate):
     assert _native.device_error() == 0
 
 
-@pytest.mark.parametrize("seq,heads", [(1000, 2), (256, 1), (77, 1)])
+@pytest.mark.parametrize("seq,heads", [(1000, 2), (256, 1), (77, 1), (1, 2), (129, 3)])
 def test_flash_matches_oracle(cuda, seq, heads):
     from slimdit import _native, attention
 

@@ -44,6 +44,15 @@ def test_full_conversion_byte_identical_to_reference(cuda, official_dir, golden_
     assert _native.device_error() == 0
 
 
+def test_sequential_path_byte_identical(cuda, official_dir, golden_meta, tmp_path):
+    """pipeline=False (ops one at a time) writes the same file as the pipelined default."""
+    from slimdit.convert import convert
+    out = tmp_path / "sequential.safetensors"
+    report = convert(official_dir, out, rank=8, grid=65, pipeline=False)
+    assert hashlib.sha256(out.read_bytes()).hexdigest() == golden_meta["convert"]["sha256_file"]
+    assert len(report.quant_errors) == len(golden_meta["convert"]["quant_errors"])
+
+
 def test_cli_entry_point(cuda, official_dir, golden_meta, tmp_path):
     from slimdit.convert import main
     out = tmp_path / "cli.safetensors"
