@@ -4,10 +4,15 @@ CPU restatement (numpy) of the reference's in-place INT8/FP8 flash attention
 (comfyui/ComfyUI-SlimDiT/attention_triton.py), used only by ``tests/``,
 ``__graft_entry__.smoke()`` and ``bench.py``'s CPU leg as the checker.
 
-Parity status: UNPINNED against the reference's Triton kernels. They need a GPU (none in
-the container that holds the reference, and the reference does not travel to the GPU
-machine), and the reference pins no outputs for them. What is restated is the algorithm as
-the reference's source states it:
+Parity status: PARTLY PINNED. The reference pins no attention outputs, its kernels are Triton
+and need a GPU, and the reference does not travel to the GPU machine. Under Triton's CPU
+interpreter (tests/golden/make_attention_golden.py) the unrotated ``quant_int8_rows`` and
+``tensor_amax`` run faithfully, and their outputs are committed golden vectors that this
+restatement (and the GPU kernels) match bit for bit. The rest is unpinned: on this image's
+interpreter ``tl.dot`` of bf16 operands returns meaningless values and the float8e4nv cast
+mis-rounds on exponent carries, so the rotated quantiser, ``quant_fp8_global`` and
+``flash_int8`` could not be run. What is restated is the algorithm as the reference's source
+states it:
 
 * quant_int8_rows (attention_triton.py:79-102): per (token, head) row of D values, optionally
   rotated by the unnormalised +-1 Sylvester Hadamard (``_hadamard``, :47-63), then

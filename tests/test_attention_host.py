@@ -161,3 +161,29 @@ def test_oracle_quality_against_dense_attention():
     dense = oa.dense_attention_f64(x, 2, D)
     cos = (got * dense).sum() / np.linalg.norm(got) / np.linalg.norm(dense)
     assert cos > 0.999
+
+
+def _golden_cases():
+    import json
+    from pathlib import Path
+
+    d = Path(__file__).resolve().parent / "golden"
+    meta = json.loads((d / "attention_quant_golden.json").read_text())
+    data = np.load(d / "attention_quant_golden.npz")
+    return meta["cases"], data
+
+
+def test_oracle_pinned_to_reference_quantiser_golden():
+    """The oracle's unrotated Q/K quantiser and V amax equal the reference's own Triton kernels
+    (quant_int8_rows with ROT=False, tensor_amax) run by tests/golden/make_attention_golden.py."""
+    cases, data = _golden_cases()
+    for c in cases:
+        key, seq, heads = c["key"], c["seq"], c["heads"]
+        x = oracle.bf16_to_f32(data[f"{key}_input_bf16"])
+        q, k, v = oa.split_packed(x, heads, D)
+        for name, t in (("q", q), ("k", k)):
+            codes, scales = oa.quant_qk(t, rotate=False)
+            assert np.array_equal(codes.reshape(seq, -1), data[f"{key}_{name}_codes"]), (key, name)
+            assert np.array_equal(scales.view(np.uint32), data[f"{key}_{name}_scales"].view(np.uint32)), (key, name)
+        _, amax = oa.quant_v(v)
+        assert np.float32(amax) == data[f"{key}_v_amax"][0], key

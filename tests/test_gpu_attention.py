@@ -212,3 +212,28 @@ def test_comfy_override_dispatch(cuda, monkeypatch):
     assert stats["kernel_calls"] == 2 and stats["fallback_calls"] == 3
     ov.uninstall()
     assert mod.optimized_attention is not ov
+
+
+def test_quantisers_match_reference_golden(cuda):
+    """Our unrotated Q/K quantiser and V amax against the reference's own Triton kernels'
+    outputs (tests/golden/attention_quant_golden.npz)."""
+    import json
+    from pathlib import Path
+
+    from slimdit import attention
+
+    d = Path(__file__).resolve().parent / "golden"
+    meta = json.loads((d / "attention_quant_golden.json").read_text())
+    data = np.load(d / "attention_quant_golden.npz")
+    for c in meta["cases"]:
+        key, seq, heads = c["key"], c["seq"], c["heads"]
+        x = oracle.bf16_to_f32(data[f"{key}_input_bf16"])
+        ops = attention.quantized_operands(to_dev(x), heads, rotate=False)
+        torch.cuda.synchronize()
+        assert np.array_equal(ops["q"].cpu().numpy(), data[f"{key}_q_codes"]), key
+        assert np.array_equal(ops["k"].cpu().numpy(), data[f"{key}_k_codes"]), key
+        assert np.array_equal(ops["q_scale"].cpu().numpy()[:, :seq].T.copy().view(np.uint32),
+                              data[f"{key}_q_scales"].view(np.uint32)), key
+        assert np.array_equal(ops["k_scale"].cpu().numpy()[:, :seq].T.copy().view(np.uint32),
+                              data[f"{key}_k_scales"].view(np.uint32)), key
+        assert ops["v_amax"].item() == float(data[f"{key}_v_amax"][0]), key
