@@ -23,6 +23,10 @@ describes (slimdit/nvfp4.py:3-15, docs/DEV_NOTES.md:59-71):
   (r, c) sits at byte (r % 32) * 16 + ((r % 128) // 32) * 4 + c % 4; tiles are ordered
   row-tile-major.
 
+Cross-check (tests/test_gpu_nvfp4.py): flashinfer's fp4_quantize, NVIDIA's NVFP4 quantiser,
+gives the same block-scale bytes in the same tiled layout and the same codes except where its
+reciprocal-multiply rounding and this recipe's division straddle a grid midpoint (one step).
+
 Nibble order: element 2i of a row goes to the LOW nibble of byte i, element 2i+1 to the
 high nibble. This is the order the tensor cores (and cuBLAS' packed E2M1 operands) read.
 The reference docstring says "high nibble first" (slimdit/nvfp4.py:5); that wording cannot

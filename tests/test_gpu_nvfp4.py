@@ -255,3 +255,37 @@ def test_converter_nvfp4_layers_match_oracle(cuda, golden_meta, tmp_path):
         assert tensor_bytes(f"{stem}.weight_scale_2") == np.float32(so).tobytes(), stem
         assert tensor_bytes(f"{stem}.comfy_quant") == b'{"format": "nvfp4"}'
     assert all(0.02 < e < 0.2 for e in report.quant_errors)
+
+
+def test_cross_check_against_flashinfer_nvfp4(cuda):
+    """Independent cross-check of the NVFP4 bytes against flashinfer's fp4_quantize (NVIDIA's
+    NVFP4 quantiser, 16-element blocks, UE4M3 scales in the 128x4 swizzled layout, global scale
+    passed as 448*6/amax): scale bytes identical; E2M1 codes identical except where the two
+    rounding sequences (x / (s2*sf) here, x * rcp(sf * rcp(1/s2)) there) straddle a grid
+    midpoint: those differ by one grid step with the same sign."""
+    flashinfer = pytest.importorskip("flashinfer")
+    import torch
+
+    from slimdit import ops
+
+    dev = torch.device("cuda", 0)
+    for m, k, seed in ((256, 512, 0), (1024, 5120, 1)):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        w = (torch.randn((m, k), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w[:, 7] *= 50
+        q, sf, s2 = ops.nvfp4_pack(w)
+        gsc = (448.0 * 6.0 / w.float().abs().max()).reshape(1).to(torch.float32)
+        fq, fsf = flashinfer.fp4_quantize(w, gsc, sf_vec_size=16, sf_use_ue8m0=False, is_sf_swizzled_layout=True)
+        torch.cuda.synchronize()
+        fq = fq.view(torch.uint8).reshape(m, k // 2).cpu().numpy()
+        fsf = fsf.view(torch.uint8).reshape(-1)[: m * k // 16].reshape(m, k // 16).cpu().numpy()
+        assert np.array_equal(sf.cpu().numpy().reshape(m, k // 16), fsf), "block scale bytes differ"
+        ours = q.cpu().numpy()
+        a = np.stack([ours & 15, ours >> 4], -1).reshape(m, k).astype(np.int16)
+        b = np.stack([fq & 15, fq >> 4], -1).reshape(m, k).astype(np.int16)
+        diff = a != b
+        assert diff.mean() < 1e-3, diff.mean()
+        # every difference: same sign, adjacent magnitudes on the E2M1 grid
+        assert np.all((a[diff] & 8) == (b[diff] & 8))
+        assert np.all(np.abs((a[diff] & 7) - (b[diff] & 7)) == 1)
