@@ -155,7 +155,8 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- inputs
 def make_inputs(torch, dev, seed: int = 0):
-    """Synthetic config-1 tensors generated on the device (same distributions as tests/synthetic.py)."""
+    """Synthetic tensors of the QKV linear (32768 x 15360 x 5120) generated on the device (same
+    distributions as tests/synthetic.py)."""
     from slimdit import ops
 
     g = torch.Generator(device=dev)
@@ -178,7 +179,7 @@ def make_inputs(torch, dev, seed: int = 0):
 
 # ----------------------------------------------------------------------------- CPU baseline
 def cpu_linear_sample(rows: int, seed: int = 0):
-    """CPU restatement of the convrot linear on `rows` tokens of the config-1 shape:
+    """CPU restatement of the convrot linear on `rows` tokens of the QKV linear (K 5120, N 15360):
     oracle rotation (C, butterfly order) + the reference's quantisation math (numpy) +
     torch's CPU int8 GEMM + fp32 dequant. Returns (seconds, threads)."""
     import numpy as np
@@ -399,14 +400,15 @@ CONVERT_SHAPES = [(15360, 5120), (5120, 5120), (13824, 5120), (5120, 13824)]  # 
 
 
 def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, reduce_max) -> dict:
-    """Config 2 (DiT FFN pair, 115200 tokens row-sharded over the ranks: strong scaling) and
-    config 4 (the converter's per-linear kernels over 40 blocks, blocks split over the ranks)."""
+    """The DiT FFN pair (115200 tokens row-sharded over the ranks: strong scaling), the
+    MiniMax-H3 linears, the NVFP4 up-projection, and the converter's per-linear kernels over 40
+    blocks (blocks split over the ranks)."""
     from slimdit import _native, ops
 
     out: dict = {}
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
-    # ---- config 2: up-proj -> GELU-tanh -> rotate + requant -> down-proj
+    # ---- DiT FFN pair: up-proj -> GELU-tanh -> rotate + requant -> down-proj
     m = (FFN_TOKENS + world - 1) // world
     g = torch.Generator(device=dev)
     g.manual_seed(100 + rank)
@@ -425,10 +427,9 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
     y = torch.empty((m, FFN_H), dtype=torch.bfloat16, device=dev)
 
     def ffn_step():
-        _native.check(lib.slim_int8_linear(x.data_ptr(), _native.BF16, qu.data_ptr(), su.data_ptr(), None, h.data_ptr(),
-                                           xq.data_ptr(), sx.data_ptr(), m, FFN_F, FFN_H, 256, _native.EPI_GELU_TANH, sp))
-        _native.check(lib.slim_int8_linear(h.data_ptr(), _native.BF16, qd.data_ptr(), sd.data_ptr(), None, y.data_ptr(),
-                                           hq.data_ptr(), sh.data_ptr(), m, FFN_H, FFN_F, 256, _native.EPI_SCALE_BIAS, sp))
+        _native.check(lib.slim_ffn_i8(x.data_ptr(), _native.BF16, qu.data_ptr(), su.data_ptr(), None, qd.data_ptr(),
+                                      sd.data_ptr(), None, y.data_ptr(), xq.data_ptr(), sx.data_ptr(), h.data_ptr(),
+                                      hq.data_ptr(), sh.data_ptr(), m, FFN_H, FFN_F, _native.EPI_GELU_TANH, sp))
 
     for _ in range(3):
         ffn_step()
@@ -498,7 +499,7 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
     del xh, xo, q1, s1, q2, s2
     torch.cuda.empty_cache()
 
-    # ---- config 3: NVFP4 up-proj (rotate + per-token NVFP4 of x, block-scaled FP4 GEMM)
+    # ---- NVFP4 up-proj (rotate + per-token NVFP4 of x, block-scaled FP4 GEMM)
     wu = (torch.randn((FFN_F, FFN_H), generator=g, device=dev) * 0.02).to(torch.bfloat16)
     pw, pws, pwg = ops.nvfp4_pack(wu)
     del wu
@@ -546,7 +547,7 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
     out["attention_packed"] = run_attention(torch, dev, lib, world, rank, steps, barrier, reduce_max)
     torch.cuda.empty_cache()
 
-    # ---- config 4: converter kernels (rotate + per-row INT8 of each block linear)
+    # ---- converter kernels (rotate + per-row INT8 of each block linear)
     my_blocks = len([i for i in range(CONVERT_BLOCKS) if i % world == rank])
     ws = [(torch.randn(shape, generator=g, device=dev) * 0.02).to(torch.bfloat16) for shape in CONVERT_SHAPES]
     qs = [torch.empty(shape, dtype=torch.int8, device=dev) for shape in CONVERT_SHAPES]
@@ -600,8 +601,8 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
     del ws, pq, psf, pts
     torch.cuda.empty_cache()
 
-    # ---- output-column split (N > 1 only): config-1 linear, weight rows split over the ranks,
-    # x replicated, column blocks all-gathered over NVLink (NCCL), "blocks" layout
+    # ---- output-column split (N > 1 only): the QKV linear (32768 x 15360 x 5120), weight rows
+    # split over the ranks, x replicated, column blocks all-gathered over NVLink (NCCL), "blocks" layout
     if world > 1:
         import torch.distributed as dist
 
@@ -639,7 +640,7 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
         ms = reduce_max(e0.elapsed_time(ends[-1]) / steps)
         gather_ms = reduce_max(sum(mids[i].elapsed_time(ends[i]) for i in range(steps)) / steps)
         out["colsplit_linear"] = {
-            "workload": f"config-1 linear, W rows split {world} ways, x replicated, NCCL all-gather of "
+            "workload": f"QKV linear 32768 x 15360 x 5120, W rows split {world} ways, x replicated, NCCL all-gather of "
                         f"[{M},{nl}] bf16 blocks ([G,M,N/G] layout)",
             "ms_per_step": round(ms, 4), "allgather_ms": round(gather_ms, 4),
             "value": round(OPS_PER_STEP / (ms * 1e-3) / 1e12, 1), "unit": "TOPS", "scaling": "strong",
@@ -664,7 +665,7 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
             torch.cuda.synchronize(dev)
             ms = reduce_max(e0.elapsed_time(ends[0]) / steps)
             out[f"colsplit_linear_peer_{mode}_{layout}"] = {
-                "workload": f"config-1 linear, W rows split {world} ways, x replicated, written into all {world} "
+                "workload": f"QKV linear 32768 x 15360 x 5120, W rows split {world} ways, x replicated, written into all {world} "
                             f"GPUs' outputs over NVLink (CUDA IPC mappings), M={M} N={N}: {what}",
                 "ms_per_step": round(ms, 4), "value": round(OPS_PER_STEP / (ms * 1e-3) / 1e12, 1), "unit": "TOPS",
                 "scaling": "strong", "nvlink_bytes_out_per_gpu": (world - 1) * M * nl * 2, "steps": steps}
@@ -708,7 +709,7 @@ def run_profile_attn(args) -> int:
 
 
 def run_profile_case(args) -> int:
-    """A small case of the config-3 NVFP4 up-proj (x [tokens, 5120] rotated + per-token
+    """A small case of the NVFP4 up-proj (x [tokens, 5120] rotated + per-token
     NVFP4, FP4 GEMM against W [13824, 5120]): warm-up + `--steps` launches of each kernel, for
     ncu captures that must stay a few GB. Prints a JSON line marked "profile_case"."""
     import torch

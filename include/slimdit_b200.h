@@ -110,6 +110,20 @@ int slim_int8_linear(const void* x, int x_dtype, const int8_t* qw, const float* 
                      const void* bias, void* out, int8_t* xq_ws, float* sx_ws, int64_t M,
                      int64_t N, int64_t K, int group, int epilogue, void* stream);
 
+/* The DiT FFN: out[M, K] = down(requant(act(up(x)))) on the device, stream-ordered, into the
+ * caller's workspaces. act = SLIM_EPI_GELU_TANH: w_up int8 [F, K] (the GELU-tanh FFN);
+ * act = SLIM_EPI_SWIGLU: w_up int8 [2F, K] with its rows interleaved per 256 (128 up rows,
+ * then the matching 128 gate rows; slimdit.ops.swiglu_interleave), the MiniMax-H3 FFN
+ * (slimdit/mapping.py:96-101). The up-projection's epilogue applies the activation to its
+ * bf16 outputs, h is rotated and requantised per token, then the down-projection w_down int8
+ * [K, F]. s_up/s_down fp32 row scales, b_up/b_down bf16 biases or NULL. Workspaces: xq_ws
+ * int8 [M, K], sx_ws fp32 [M], h_ws bf16 [M, F], hq_ws int8 [M, F], sh_ws fp32 [M]. */
+int slim_ffn_i8(const void* x, int x_dtype, const int8_t* w_up, const float* s_up,
+                const void* b_up, const int8_t* w_down, const float* s_down,
+                const void* b_down, void* out, int8_t* xq_ws, float* sx_ws, void* h_ws,
+                int8_t* hq_ws, float* sh_ws, int64_t M, int64_t K, int64_t F, int act,
+                void* stream);
+
 /* The convrot linear without caller workspaces, for callers that cannot allocate device
  * memory: code running inside a host framework that owns the device memory pool (a plugin
  * given only its inputs and outputs), or on a path where an allocation would synchronise
@@ -182,7 +196,7 @@ int slim_nvfp4_pack(const void* w, int dtype, int64_t rows, int64_t K, uint8_t* 
  * (row_scale fp32 [rows]), optionally after the group-256 Hadamard rotation in the
  * butterfly order (rotate != 0; K % 256 == 0). q: uint8 [rows, K/2]; block_scale: uint8
  * [round_up(rows, 128), K/16] (padding rows get zero scales). The input side of the NVFP4
- * runtime linear that consumes slimdit/nvfp4.py's format. */
+ * runtime linear that consumes slimdit/nvfp4.py's format (the NVFP4 up-projection). */
 int slim_quant_nvfp4_act(const void* x, int dtype, int64_t rows, int64_t K, int rotate,
                          uint8_t* q, uint8_t* block_scale, float* row_scale, void* stream);
 

@@ -10,7 +10,7 @@ inputs (tests/synthetic.py):
     5120, 13824 (every OpenBLAS order the reference's rotation goes through);
   * dequantize_convrot_weight outputs;
   * per-token activation quantisation with the reference's own math (rotate + int8.py:49-51);
-  * SHA-256 of the full config-0 weight conversion (W [5120, 5120]);
+  * SHA-256 of the full weight conversion of W [5120, 5120];
   * the descriptor blob, and the bytes (SHA-256 + header) of reference convert() runs on a
     2-block synthetic official checkpoint (full, and with block_limit=0);
   * the NVFP4 host contract of slimdit/nvfp4.py that needs no comfy_kitchen: descriptor

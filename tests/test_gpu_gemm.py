@@ -228,3 +228,41 @@ def test_swiglu_epilogue_and_minimax_ffn(cuda):
     assert torch.equal(yf, ref_f)
     with pytest.raises(ValueError):  # rows not a multiple of 256
         ops.swiglu_interleave(q1d[:384], s1d[:384])
+
+
+@pytest.mark.parametrize("act", ["gelu_tanh", "swiglu"])
+@pytest.mark.parametrize("lead", [(1,), (3,), (2, 130), (1000,)])
+def test_ffn_c_entry_equals_two_linears(cuda, act, lead):
+    """slim_ffn_i8 (one C call: up-proj with the activation epilogue, rotate + requant, down-proj)
+    gives the same bytes as the two convrot linears run one after the other, biases included."""
+    from slimdit import _native as nat
+    from slimdit import ops
+    from slimdit.int8 import quantize_convrot_weight
+    hdim, f = 512, 768
+    n_up = 2 * f if act == "swiglu" else f
+    rows = int(np.prod(lead))
+    x = synthetic.activations(rows, hdim, seed=51 + rows)
+    qu, su = quantize_convrot_weight(synthetic.weight(n_up, hdim, seed=52))
+    qd, sd = quantize_convrot_weight(synthetic.weight(hdim, f, seed=53))
+    rng = np.random.default_rng(54)
+    bu = torch.from_numpy(rng.standard_normal(n_up).astype(np.float32) * 0.02).to(cuda).to(torch.bfloat16)
+    bd = torch.from_numpy(rng.standard_normal(hdim).astype(np.float32) * 0.02).to(cuda).to(torch.bfloat16)
+    xt = torch.from_numpy(x).to(cuda).to(torch.bfloat16).reshape(*lead, hdim)
+    qud, sud = torch.from_numpy(qu).to(cuda), torch.from_numpy(su).to(cuda)
+    qdd, sdd = torch.from_numpy(qd).to(cuda), torch.from_numpy(sd).to(cuda)
+    if act == "swiglu":
+        qud, sud, bu = ops.swiglu_interleave(qud, sud, bu)
+        y = ops.ffn_swiglu_int8(xt, qud, sud, qdd, sdd, bu, bd)
+    else:
+        y = ops.ffn_int8(xt, qud, sud, qdd, sdd, bu, bd)
+    h = ops.int8_linear(xt, qud, sud, bias=bu, epilogue=act)
+    ref = ops.int8_linear(h, qdd, sdd, bias=bd)
+    assert y.shape == (*lead, hdim) and torch.equal(y, ref)
+    # the C entry rejects an activation that is not an FFN's
+    z = torch.empty(1, device=cuda)
+    rc = nat.load().slim_ffn_i8(xt.data_ptr(), 1, qud.data_ptr(), sud.data_ptr(), None, qdd.data_ptr(),
+                                sdd.data_ptr(), None, z.data_ptr(), z.data_ptr(), z.data_ptr(), z.data_ptr(),
+                                z.data_ptr(), z.data_ptr(), rows, hdim, f, nat.EPI_SCALE_BIAS, 0)
+    assert rc != 0
+    with pytest.raises(ValueError):
+        ops.ffn_int8(xt, qdd, sdd, qud, sud)

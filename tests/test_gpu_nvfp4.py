@@ -1,4 +1,4 @@
-"""GPU parity of the NVFP4 path (slimdit/nvfp4.py format) through the C ABI.
+"""GPU parity of the NVFP4 path (slimdit/nvfp4.py format, the NVFP4 up-projection) through the C ABI.
 
 * weight packing and activation quantisation: packed codes, tiled block-scale bytes and
   global scales bit-exact with the oracle's restatement (oracle/nvfp4.py);

@@ -57,7 +57,7 @@ def test_dequantize_bit_exact_vs_reference(cuda, golden, name):
 
 
 def test_config0_full_weight_bit_exact(cuda, golden_meta):
-    """Config 0: W bf16 [5120, 5120] ~ N(0, 0.02), 5 outlier channels x50 -> codes and scales
+    """The 5120 x 5120 weight: W bf16 [5120, 5120] ~ N(0, 0.02), 5 outlier channels x50 -> codes and scales
     identical to the reference's quantize_convrot_weight (SHA-256)."""
     from slimdit import ops
     meta = golden_meta["config0"]

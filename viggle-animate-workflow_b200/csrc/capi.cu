@@ -241,6 +241,25 @@ int slim_int8_linear(const void* x, int x_dtype, const int8_t* qw, const float* 
   return SLIM_OK;
 }
 
+int slim_ffn_i8(const void* x, int x_dtype, const int8_t* w_up, const float* s_up, const void* b_up,
+                const int8_t* w_down, const float* s_down, const void* b_down, void* out, int8_t* xq_ws,
+                float* sx_ws, void* h_ws, int8_t* hq_ws, float* sh_ws, int64_t M, int64_t K, int64_t F, int act,
+                void* stream) {
+  if (act != kEpiGeluTanh && act != kEpiSwiGLU)
+    return fail(SLIM_ERR_DTYPE, "FFN activation must be GELU-tanh (%d) or SwiGLU (%d), got %d", kEpiGeluTanh,
+                kEpiSwiGLU, act);
+  if (F <= 0 || K <= 0 || M < 0) return fail(SLIM_ERR_SHAPE, "bad FFN shape M=%lld K=%lld F=%lld",
+                                             static_cast<long long>(M), static_cast<long long>(K),
+                                             static_cast<long long>(F));
+  // up-projection: [M, K] x [F or 2F, K]^T with the activation in the epilogue -> h bf16 [M, F]
+  const int64_t n_up = act == kEpiSwiGLU ? 2 * F : F;
+  int rc = slim_int8_linear(x, x_dtype, w_up, s_up, b_up, h_ws, xq_ws, sx_ws, M, n_up, K, 256, act, stream);
+  if (rc != SLIM_OK) return rc;
+  // down-projection: h rotated and requantised per token, [M, F] x [K, F]^T -> out bf16 [M, K]
+  return slim_int8_linear(h_ws, SLIM_BF16, w_down, s_down, b_down, out, hq_ws, sh_ws, M, K, F, 256, kEpiScaleBias,
+                          stream);
+}
+
 int slim_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
   if (ptr == nullptr || ipc_handle == nullptr) return fail(SLIM_ERR_NULL, "ptr/ipc_handle is NULL");
   if (bytes == 0) return fail(SLIM_ERR_SHAPE, "empty peer buffer");
