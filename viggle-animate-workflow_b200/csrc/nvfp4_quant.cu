@@ -53,25 +53,41 @@ __device__ __forceinline__ uint32_t e2m1_code(float v) {
   return c | ((__float_as_uint(v) >> 28) & 8u);
 }
 
-// E2M1 magnitude code of a >= 0 by region scaling: the grid has step 1/2 below 2, 1 in
-// [2, 4) and 2 above, so code = base + rint(a * scale) with (scale, base) = (2, 0), (1, 2),
-// (1/2, 4), saturating at 7. rint (round half to even on a*scale, exact since the scales are
-// powers of two) gives exactly the grid's half-to-even ties: 0.25 -> 0, 0.75 -> 1.0,
-// 1.25 -> 1.0, 1.75 -> 2.0, 2.5 -> 2.0, 3.5 -> 4.0, 5 -> 4.0. `frac` returns |a*scale - rint|.
-__device__ __forceinline__ uint32_t e2m1_mag(float a, float& frac) {
-  const float scale = a < 2.0f ? 2.0f : (a < 4.0f ? 1.0f : 0.5f);
-  const uint32_t base = a < 2.0f ? 0u : (a < 4.0f ? 2u : 4u);
-  const float s = __fmul_rn(a, scale);
-  const float r = rintf(s);
-  frac = fabsf(__fsub_rn(s, r));
-  return min(base + static_cast<uint32_t>(r), 7u);
+// Two fp32 products, each rounded once: {a.x*b.x, a.y*b.y} (one packed instruction).
+__device__ __forceinline__ float2 mul_rn_x2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// Eight values -> eight E2M1 codes in one word, value 2i in the low nibble of byte i: the
+// hardware conversion rounds to the nearest grid point and saturates at 6 (ties never reach
+// it here, see quant_block16); the sign is the value's.
+__device__ __forceinline__ uint32_t e2m1x8(const float2 (&t)[4]) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(r)
+      : "f"(t[0].x), "f"(t[0].y), "f"(t[1].x), "f"(t[1].y), "f"(t[2].x), "f"(t[2].y), "f"(t[3].x), "f"(t[3].y));
+  return r;
 }
 
 // One 16-element block -> 8 packed bytes and its scale byte.
-// The element quotient v = fl(x / total) is not formed: t = |x| * fl(1/total) is within
-// 2^-22 |v| of |v| (two roundings), so e2m1_mag(t) equals e2m1_mag(|v|) unless t*scale lies
-// within 2^-18 of a half-integer (a rounding boundary); those elements (about 1e-5 of them)
-// take the IEEE division. The sign is x's (a zero quotient keeps x's sign, as the division's).
+// The element quotient v = fl(x / total) is not formed. With r = fl(1/total), the products
+// hi = fl(x * fl(r (1 + 2^-19))) and lo = fl(x * fl(r (1 - 2^-19))) bracket v in magnitude
+// (three roundings move each by at most 3 * 2^-24 relative, well inside the 2^-19 offset), and
+// the E2M1 code is monotone in |v| with the sign apart, so where the codes of hi and lo agree
+// they are v's code. Where they differ (v within ~2^-19 of a rounding boundary, including every
+// exact tie: about 1e-5 of the elements) the IEEE division decides; so does every element of a
+// block whose reciprocal is not finite. The sign is x's (a zero quotient keeps x's sign, as
+// the division's).
 __device__ __forceinline__ void quant_block16(const float (&v)[16], float gs, uint2& packed, uint32_t& sfb) {
   float bm = 0.0f;
 #pragma unroll
@@ -85,20 +101,29 @@ __device__ __forceinline__ void quant_block16(const float (&v)[16], float gs, ui
   uint32_t w[2] = {0u, 0u};
   if (total != 0.0f) {
     const float rcp = __frcp_rn(total);
-    uint32_t slow = 0;
+    uint32_t d[2] = {0xffffffffu, 0xffffffffu};
+    if (rcp <= 3.402823466e38f) {
+      const float rh = __fmul_rn(rcp, 1.0f + 1.9073486328125e-6f);
+      const float rl = __fmul_rn(rcp, 1.0f - 1.9073486328125e-6f);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float frac;
-      const uint32_t mag = e2m1_mag(__fmul_rn(fabsf(v[i]), rcp), frac);
-      slow |= static_cast<uint32_t>(frac > 0.5f - 7.62939453125e-6f) << i;  // 2^-17 margin
-      w[i >> 3] |= (mag | ((__float_as_uint(v[i]) >> 28) & 8u)) << (4 * (i & 7));
+      for (int h = 0; h < 2; ++h) {
+        float2 th[4], tl[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 x2 = make_float2(v[8 * h + 2 * j], v[8 * h + 2 * j + 1]);
+          th[j] = mul_rn_x2(x2, make_float2(rh, rh));
+          tl[j] = mul_rn_x2(x2, make_float2(rl, rl));
+        }
+        w[h] = e2m1x8(th);
+        d[h] = w[h] ^ e2m1x8(tl);
+      }
     }
-    if (slow != 0u) {
+    if ((d[0] | d[1]) != 0u) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        if ((slow >> i) & 1u) {
+        const uint32_t sh = 4 * (i & 7);
+        if ((d[i >> 3] >> sh) & 15u) {
           const uint32_t code = e2m1_code(__fdiv_rn(v[i], total));
-          const uint32_t sh = 4 * (i & 7);
           w[i >> 3] = (w[i >> 3] & ~(15u << sh)) | (code << sh);
         }
       }
