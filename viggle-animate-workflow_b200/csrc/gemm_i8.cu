@@ -15,8 +15,12 @@
 //               lane issues tcgen05.mma (M=128, N=256, K=32 per instruction, 4 per stage),
 //               committing to the ring's empty barriers and to the accumulator barriers.
 //   warps 2..5  epilogue: tcgen05.ld of the accumulator rows (warp w owns TMEM lanes
-//               32*(w%4)..+31), scale/bias/GELU in fp32, bf16 stores; double-buffered
-//               accumulators let the next tile's MMAs run under this epilogue.
+//               32*(w%4)..+31), scale/bias/GELU in fp32, bf16 rows staged in shared memory
+//               and written back with each store instruction covering four 128-byte row
+//               segments; double-buffered accumulators let the next tile's MMAs run under
+//               this epilogue. (Stored straight from the registers, one row per thread, the
+//               16-byte writes of 32 rows per instruction slowed the MMAs sharing the SM's
+//               load/store path: 2.14 vs 2.01 ms at 32768 x 15360 x 5120.)
 // Every mbarrier wait is bounded (slim_ptx.cuh); on a timeout the kernel records an error,
 // drains its own TMA loads and MMAs, frees TMEM and returns.
 #include <cuda.h>
@@ -43,6 +47,9 @@ constexpr int GROUP_M = 16;
 constexpr int MMA_K = 32;
 constexpr uint32_t IDESC = idesc_i8(BM, BN);
 
+constexpr int EPI_WARPS = 4;
+constexpr int STAGING_BYTES = 32 * 128;  // per epilogue warp: 32 rows x 64 bf16
+
 struct Shared {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
@@ -53,7 +60,9 @@ struct Shared {
   volatile int abort;
 };
 
-constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + sizeof(Shared) + 64;
+constexpr size_t SMEM_BYTES =
+    1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + EPI_WARPS * STAGING_BYTES + sizeof(Shared) + 64;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 __device__ __forceinline__ void tile_coords(int64_t t, int tiles_m, int tiles_n, int& tm, int& tn) {
   const int64_t per_group = static_cast<int64_t>(GROUP_M) * tiles_n;
@@ -107,13 +116,46 @@ __device__ __forceinline__ void linear8(const GemmI8Params& p, const uint32_t* r
     y[e] = bf16_round(__fmaf_rn(static_cast<float>(static_cast<int>(r[e])), sam * sv[e], bv[e]));
 }
 
+// Write-back of one slice of a warp's 32 output rows: lane i holds row m0 + i's ROW_BYTES
+// bytes of bf16 (w). The rows go to shared memory (16-byte chunk j of row r at chunk position
+// j ^ swz(r), so that neither the row-wise writes nor the column-wise reads conflict), then each
+// store instruction writes 512 contiguous-by-row bytes: 4 rows x 128 bytes (ROW_BYTES 128) or
+// 8 rows x 64 bytes (ROW_BYTES 64). Rows >= M and columns >= N are skipped; the same bytes go to
+// every peer destination. All 32 lanes must call it.
+template <int ROW_BYTES>
+__device__ __forceinline__ void store_slice(const GemmI8Params& p, uint8_t* stg, const uint32_t* w, int64_t m0,
+                                            int64_t n0, int lane) {
+  constexpr int CH = ROW_BYTES / 16;           // 16-byte chunks per row
+  constexpr int RPI = 32 / CH;                 // rows per store instruction
+  auto swz = [](int r) { return CH == 8 ? (r & 7) : ((r >> 1) & 3); };
+  uint4* srow = reinterpret_cast<uint4*>(stg + lane * ROW_BYTES);
+#pragma unroll
+  for (int j = 0; j < CH; ++j) srow[j ^ swz(lane)] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+  __syncwarp();
+  const int j = lane % CH;
+  const bool col_ok = n0 + 8 * j < p.N;
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+    const int r = RPI * i + lane / CH;
+    const uint4 v = reinterpret_cast<const uint4*>(stg + r * ROW_BYTES)[j ^ swz(r)];
+    const int64_t m = m0 + r;
+    if (col_ok && m < p.M) {
+      const int64_t off = m * p.ldo + n0 + 8 * j;
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + off) = v;
+#pragma unroll
+      for (int d = 0; d < kMaxPeers; ++d)
+        if (d < p.n_peer) *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.peer_out[d]) + off) = v;
+    }
+  }
+  __syncwarp();  // the staging rows are read before the next slice overwrites them
+}
+
 // SwiGLU epilogue: the weight rows are interleaved per 256-row tile (128 "up" rows, then the 128
 // matching "gate" rows), so the tile's columns [0,128) and [128,256) pair up; the output
 // column n_base/2 + i gets bf16(up * bf16(silu(gate))), with up and gate the bf16 linear
 // outputs: the roundings of running the linear in bf16 and then ComfyUI's swiglu on its output.
-__device__ __forceinline__ void epilogue_rows_swiglu(const GemmI8Params& p, uint32_t tbase, int64_t m, bool row_ok,
-                                                     float sam, int64_t n_base) {
-  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+__device__ __forceinline__ void epilogue_rows_swiglu(const GemmI8Params& p, uint32_t tbase, int64_t m0, int lane,
+                                                     float sam, int64_t n_base, uint8_t* stg) {
   const int64_t o_base = n_base / 2;
 #pragma unroll 1
   for (int c = 0; c < BN / 64; ++c) {
@@ -122,7 +164,8 @@ __device__ __forceinline__ void epilogue_rows_swiglu(const GemmI8Params& p, uint
     tmem_ld_32x32b_x32(tbase + BN / 2 + c * 32, rg);
     tmem_ld_wait();
     const int64_t nu = n_base + c * 32, ng = n_base + BN / 2 + c * 32;
-    if (!row_ok || nu >= p.N) continue;
+    if (nu >= p.N) continue;  // warp-uniform
+    uint32_t w[16];
 #pragma unroll
     for (int j = 0; j < 32; j += 8) {
       float up[8], g[8];
@@ -134,77 +177,74 @@ __device__ __forceinline__ void epilogue_rows_swiglu(const GemmI8Params& p, uint
         const float sl = bf16_round(__fdiv_rn(g[e], __fadd_rn(1.0f, expf(-g[e]))));
         y[e] = __fmul_rn(up[e], sl);
       }
-      uint4 o;
-      o.x = pack_bf16x2(y[0], y[1]);
-      o.y = pack_bf16x2(y[2], y[3]);
-      o.z = pack_bf16x2(y[4], y[5]);
-      o.w = pack_bf16x2(y[6], y[7]);
-      *reinterpret_cast<uint4*>(out + m * p.ldo + o_base + c * 32 + j) = o;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w[j / 2 + e] = pack_bf16x2(y[2 * e], y[2 * e + 1]);
     }
+    store_slice<64>(p, stg, w, m0, o_base + c * 32, lane);
   }
 }
 
-// One accumulator tile row-slice: this thread's row m (TMEM lane), 256 columns from n_base,
-// read 32 columns at a time; scale/bias(/GELU) in fp32, bf16 stores, optional int32 copy.
-// All 32 lanes of the warp must call it (tcgen05.ld is warp-collective).
-__device__ __forceinline__ void epilogue_rows(const GemmI8Params& p, uint32_t tbase, int64_t m, bool row_ok,
-                                              float sam, int64_t n_base) {
+// One accumulator tile row-slice: this thread's row m0 + lane (TMEM lane), 256 columns from
+// n_base, read 64 columns at a time; scale/bias(/GELU) in fp32, bf16 rows written back through
+// the warp's staging buffer `stg`, optional int32 copy. All 32 lanes of the warp must call it
+// (tcgen05.ld is warp-collective).
+__device__ __forceinline__ void epilogue_rows(const GemmI8Params& p, uint32_t tbase, int64_t m0, int lane,
+                                              bool row_ok, float sam, int64_t n_base, uint8_t* stg) {
   if (p.epilogue == kEpiSwiGLU) {
-    epilogue_rows_swiglu(p, tbase, m, row_ok, sam, n_base);
+    epilogue_rows_swiglu(p, tbase, m0, lane, sam, n_base, stg);
     return;
   }
+  const int64_t m = m0 + lane;
   const __nv_bfloat16* bias = static_cast<const __nv_bfloat16*>(p.bias);
-  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; ++c) {
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(tbase + c * 32, r);
+  for (int c = 0; c < BN / 64; ++c) {
+    uint32_t r[64];
+    tmem_ld_32x32b_x32(tbase + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+    tmem_ld_32x32b_x32(tbase + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
     tmem_ld_wait();
-    const int64_t n0 = n_base + c * 32;
-    if (row_ok) {
-      if (p.acc_dbg != nullptr) {
-        int32_t* dst = p.acc_dbg + m * p.N + n0;
+    const int64_t n0 = n_base + c * 64;
+    if (n0 >= p.N) continue;  // warp-uniform
+    if (row_ok && p.acc_dbg != nullptr) {
+      int32_t* dst = p.acc_dbg + m * p.N + n0;
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          if (n0 + j < p.N)
-            *reinterpret_cast<int4*>(dst + j) = make_int4(static_cast<int>(r[j]), static_cast<int>(r[j + 1]),
-                                                          static_cast<int>(r[j + 2]), static_cast<int>(r[j + 3]));
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        if (n0 + j >= p.N) break;
-        const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j));
-        const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j + 4));
-        const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-        float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (bias != nullptr) {
-          const uint4 bu = __ldg(reinterpret_cast<const uint4*>(bias + n0 + j));
-          const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            bv[2 * e] = __uint_as_float(bw[e] << 16);
-            bv[2 * e + 1] = __uint_as_float(bw[e] & 0xffff0000u);
-          }
-        }
-        float y[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float acc = static_cast<float>(static_cast<int>(r[j + e]));
-          y[e] = __fmaf_rn(acc, sam * sv[e], bv[e]);
-          if (p.epilogue == kEpiGeluTanh) y[e] = gelu_tanh(bf16_round(y[e]));
-        }
-        uint4 o;
-        o.x = pack_bf16x2(y[0], y[1]);
-        o.y = pack_bf16x2(y[2], y[3]);
-        o.z = pack_bf16x2(y[4], y[5]);
-        o.w = pack_bf16x2(y[6], y[7]);
-        *reinterpret_cast<uint4*>(out + m * p.ldo + n0 + j) = o;
-#pragma unroll
-        for (int d = 0; d < kMaxPeers; ++d)
-          if (d < p.n_peer) *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.peer_out[d]) + m * p.ldo + n0 + j) = o;
+      for (int j = 0; j < 64; j += 4) {
+        if (n0 + j < p.N)
+          *reinterpret_cast<int4*>(dst + j) = make_int4(static_cast<int>(r[j]), static_cast<int>(r[j + 1]),
+                                                        static_cast<int>(r[j + 2]), static_cast<int>(r[j + 3]));
       }
     }
+    uint32_t w[32];
+#pragma unroll
+    for (int j = 0; j < 64; j += 8) {
+      if (n0 + j >= p.N) {  // past the last column (N % 8 == 0): nothing of these 8 is stored
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[j / 2 + e] = 0u;
+        continue;
+      }
+      const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j));
+      const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j + 4));
+      const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (bias != nullptr) {
+        const uint4 bu = __ldg(reinterpret_cast<const uint4*>(bias + n0 + j));
+        const uint32_t bw[4] = {bu.x, bu.y, bu.z, bu.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          bv[2 * e] = __uint_as_float(bw[e] << 16);
+          bv[2 * e + 1] = __uint_as_float(bw[e] & 0xffff0000u);
+        }
+      }
+      float y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float acc = static_cast<float>(static_cast<int>(r[j + e]));
+        y[e] = __fmaf_rn(acc, sam * sv[e], bv[e]);
+        if (p.epilogue == kEpiGeluTanh) y[e] = gelu_tanh(bf16_round(y[e]));
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w[j / 2 + e] = pack_bf16x2(y[2 * e], y[2 * e + 1]);
+    }
+    store_slice<128>(p, stg, w, m0, n0, lane);
   }
 }
 
@@ -216,7 +256,8 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
   uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  Shared& sh = *reinterpret_cast<Shared*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* staging = smem + STAGES * STAGE_BYTES;
+  Shared& sh = *reinterpret_cast<Shared*>(staging + EPI_WARPS * STAGING_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -327,7 +368,6 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
   } else {
     // epilogue warps 2..5
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
     int as = 0;
     uint32_t aphase = 0;
     for (int64_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
@@ -340,12 +380,13 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
       tc_fence_after();
       int tm, tn;
       tile_coords(t, tiles_m, tiles_n, tm, tn);
-      const int64_t m = static_cast<int64_t>(tm) * BM + row;
-      const bool row_ok = m < p.M;
-      const float sam = row_ok ? __ldg(p.sa + m) : 0.0f;
+      const int64_t m0 = static_cast<int64_t>(tm) * BM + quarter * 32;
+      const bool row_ok = m0 + lane < p.M;
+      const float sam = row_ok ? __ldg(p.sa + m0 + lane) : 0.0f;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(as * BN);
-      epilogue_rows(p, tbase, m, row_ok, sam, static_cast<int64_t>(tn) * BN);
+      epilogue_rows(p, tbase, m0, lane, row_ok, sam, static_cast<int64_t>(tn) * BN,
+                    staging + (warp - 2) * STAGING_BYTES);
       tc_fence_before();
       mbar_arrive(&sh.tempty[as]);
       as ^= 1;
@@ -391,7 +432,9 @@ struct SharedP {
   uint32_t tmem_base;
   volatile int abort;
 };
-constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + sizeof(SharedP) + 64;
+constexpr size_t SMEM_BYTES =
+    1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + EPI_WARPS * STAGING_BYTES + sizeof(SharedP) + 64;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 __device__ __forceinline__ void tile_coords2(int64_t t, int tiles_m, int tiles_n, int& tm, int& tn) {
   const int64_t per_group = static_cast<int64_t>(GROUP_M2) * tiles_n;
@@ -412,7 +455,8 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
   uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  SharedP& sh = *reinterpret_cast<SharedP*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* staging = smem + STAGES * STAGE_BYTES;
+  SharedP& sh = *reinterpret_cast<SharedP*>(staging + EPI_WARPS * STAGING_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -534,7 +578,6 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
     __syncwarp();
   } else {
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
     int as = 0;
     uint32_t aphase = 0;
     for (int64_t t = pair_id; t < total_tiles; t += npairs) {
@@ -547,12 +590,13 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
       tc_fence_after();
       int tm, tn;
       tile_coords2(t, tiles_m, tiles_n, tm, tn);
-      const int64_t m = static_cast<int64_t>(tm) * (2 * BM) + static_cast<int64_t>(rank) * BM + row;
-      const bool row_ok = m < p.M;
-      const float sam = row_ok ? __ldg(p.sa + m) : 0.0f;
+      const int64_t m0 = static_cast<int64_t>(tm) * (2 * BM) + static_cast<int64_t>(rank) * BM + quarter * 32;
+      const bool row_ok = m0 + lane < p.M;
+      const float sam = row_ok ? __ldg(p.sa + m0 + lane) : 0.0f;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(as * BN);
-      epilogue_rows(p, tbase, m, row_ok, sam, static_cast<int64_t>(tn) * BN);
+      epilogue_rows(p, tbase, m0, lane, row_ok, sam, static_cast<int64_t>(tn) * BN,
+                    staging + (warp - 2) * STAGING_BYTES);
       tc_fence_before();
       mbar_arrive_cluster(mapa_shared(smem_u32(&sh.tempty[as]), 0));
       as ^= 1;
