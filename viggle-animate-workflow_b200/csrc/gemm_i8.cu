@@ -116,38 +116,48 @@ __device__ __forceinline__ void linear8(const GemmI8Params& p, const uint32_t* r
     y[e] = bf16_round(__fmaf_rn(static_cast<float>(static_cast<int>(r[e])), sam * sv[e], bv[e]));
 }
 
-// Write-back of one slice of a warp's 32 output rows: lane i holds row m0 + i's ROW_BYTES
-// bytes of bf16 (w). The rows go to shared memory (16-byte chunk j of row r at chunk position
-// j ^ swz(r), so that neither the row-wise writes nor the column-wise reads conflict), then each
-// store instruction writes 512 contiguous-by-row bytes: 4 rows x 128 bytes (ROW_BYTES 128) or
-// 8 rows x 64 bytes (ROW_BYTES 64). Rows >= M and columns >= N are skipped; the same bytes go to
-// every peer destination. All 32 lanes must call it.
+// Write-back of one slice of a warp's 32 bf16 output rows [m0, m0+32) x [n0, n0 + ROW_BYTES/2):
+// lane i holds row m0 + i's ROW_BYTES bytes (w). The rows go to the warp's staging buffer in
+// shared memory (16-byte chunk j of row r at chunk position j ^ ((r / (8/CH)) % CH), so that
+// neither the row-wise writes nor the column-wise reads conflict), then each store instruction
+// writes 32 x 16 bytes as whole row segments: 4 rows x 128 bytes, 8 x 64 or 16 x 32. Rows >= M
+// and columns >= N are skipped; the same bytes go to each of the n_peer further destinations.
+// All 32 lanes must call it.
 template <int ROW_BYTES>
-__device__ __forceinline__ void store_slice(const GemmI8Params& p, uint8_t* stg, const uint32_t* w, int64_t m0,
-                                            int64_t n0, int lane) {
-  constexpr int CH = ROW_BYTES / 16;           // 16-byte chunks per row
-  constexpr int RPI = 32 / CH;                 // rows per store instruction
-  auto swz = [](int r) { return CH == 8 ? (r & 7) : ((r >> 1) & 3); };
+__device__ __forceinline__ void store_rows_staged(__nv_bfloat16* out, void* const* peers, int n_peer, int64_t ldo,
+                                                  int64_t M, int64_t N, uint8_t* stg, const uint32_t* w, int64_t m0,
+                                                  int64_t n0, int lane) {
+  constexpr int CH = ROW_BYTES / 16;  // 16-byte chunks per row
+  constexpr int RPI = 32 / CH;        // rows per store instruction
+  static_assert(CH == 2 || CH == 4 || CH == 8, "row slice of 32, 64 or 128 bytes");
+  auto swz = [](int r) { return (r / (8 / CH)) % CH; };
   uint4* srow = reinterpret_cast<uint4*>(stg + lane * ROW_BYTES);
 #pragma unroll
   for (int j = 0; j < CH; ++j) srow[j ^ swz(lane)] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
   __syncwarp();
   const int j = lane % CH;
-  const bool col_ok = n0 + 8 * j < p.N;
+  const bool col_ok = n0 + 8 * j < N;
 #pragma unroll
   for (int i = 0; i < CH; ++i) {
     const int r = RPI * i + lane / CH;
     const uint4 v = reinterpret_cast<const uint4*>(stg + r * ROW_BYTES)[j ^ swz(r)];
     const int64_t m = m0 + r;
-    if (col_ok && m < p.M) {
-      const int64_t off = m * p.ldo + n0 + 8 * j;
-      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + off) = v;
+    if (col_ok && m < M) {
+      const int64_t off = m * ldo + n0 + 8 * j;
+      *reinterpret_cast<uint4*>(out + off) = v;
 #pragma unroll
       for (int d = 0; d < kMaxPeers; ++d)
-        if (d < p.n_peer) *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.peer_out[d]) + off) = v;
+        if (d < n_peer) *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(peers[d]) + off) = v;
     }
   }
   __syncwarp();  // the staging rows are read before the next slice overwrites them
+}
+
+template <int ROW_BYTES>
+__device__ __forceinline__ void store_slice(const GemmI8Params& p, uint8_t* stg, const uint32_t* w, int64_t m0,
+                                            int64_t n0, int lane) {
+  store_rows_staged<ROW_BYTES>(static_cast<__nv_bfloat16*>(p.out), p.peer_out, p.n_peer, p.ldo, p.M, p.N, stg, w, m0,
+                               n0, lane);
 }
 
 // SwiGLU epilogue: the weight rows are interleaved per 256-row tile (128 "up" rows, then the 128

@@ -28,7 +28,12 @@
 //                the columns to the MMA warp.
 //   warps 6..13  epilogue: each warp reads 128 accumulator columns of its lane quarter,
 //                scales + biases them (GELU if asked) and packs bf16 in registers, releases the
-//                accumulator to the next tile's MMAs, then stores.
+//                accumulator to the next tile's MMAs, then writes its 32 rows back through a
+//                1 KB shared-memory buffer, 16 columns at a time, each store instruction
+//                covering 16 rows x 32 bytes. (One row per thread, the 16-byte stores into 32
+//                rows per instruction slowed the MMAs by ~12 %; the ring leaves no room for a
+//                wider buffer, and moving the scale atoms out of the ring to make room put
+//                their global-memory latency in front of the MMAs.)
 // Every mbarrier wait is bounded; on a timeout the kernel records an error, drains its
 // copies and MMAs, frees TMEM and returns.
 #include <cuda.h>
@@ -46,6 +51,8 @@ constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BKB = 128;                  // bytes of packed FP4 per row per k-block (256 elements)
 constexpr int STAGES = 4;
+constexpr int EPI_ROW_BYTES = 32;         // bf16 bytes per row of one write-back slice (16 columns)
+constexpr int STAGING_BYTES = 32 * EPI_ROW_BYTES;  // per epilogue warp: what the ring leaves free
 constexpr int A_BYTES = BM * BKB;         // 16 KB
 constexpr int B_BYTES = BN * BKB;         // 32 KB
 constexpr int ATOM = 512;                 // one 128-row x 4-scale tile of the block-scale layout
@@ -73,7 +80,8 @@ struct Shared {
   volatile int abort;
 };
 
-constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + sizeof(Shared) + 64;
+constexpr size_t SMEM_BYTES =
+    1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + 8 * STAGING_BYTES + sizeof(Shared) + 64;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 static_assert(SF_COL0 + STAGES * SF_COLS <= TMEM_COLS, "TMEM budget");
 
@@ -97,7 +105,8 @@ gemm_nvf4_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
   uint8_t* sB = sA + STAGES * A_BYTES;
   uint8_t* sFA = sB + STAGES * B_BYTES;
   uint8_t* sFB = sFA + STAGES * SFA_BYTES;
-  Shared& sh = *reinterpret_cast<Shared*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* staging = smem + STAGES * STAGE_BYTES;
+  Shared& sh = *reinterpret_cast<Shared*>(staging + 8 * STAGING_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -319,10 +328,13 @@ gemm_nvf4_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
       tc_fence_before();
       mbar_arrive(&sh.tempty);  // the accumulator is in registers: the next tile may start
       aphase ^= 1;
-      if (row_ok && cols_ok) {
-        uint4* dst = reinterpret_cast<uint4*>(out + m * p.ldo + nbase);
+      if (cols_ok) {  // warp-uniform
+        const int64_t m0 = static_cast<int64_t>(tm) * BM + quarter * 32;
+        uint8_t* stg = staging + (warp - EPI_WARP0) * STAGING_BYTES;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        for (int c = 0; c < 256 / EPI_ROW_BYTES; ++c)
+          gi8::store_rows_staged<EPI_ROW_BYTES>(out, nullptr, 0, p.ldo, p.M, p.N, stg, pk + c * (EPI_ROW_BYTES / 4), m0,
+                                                nbase + c * (EPI_ROW_BYTES / 2), lane);
       }
     }
   }
