@@ -16,17 +16,20 @@
 //               committing to the ring's empty barriers and to the accumulator barriers.
 //   warps 2..5  epilogue: tcgen05.ld of the accumulator rows (warp w owns TMEM lanes
 //               32*(w%4)..+31), scale/bias/GELU in fp32, bf16 rows staged in shared memory
-//               and written back with each store instruction covering four 128-byte row
-//               segments; double-buffered accumulators let the next tile's MMAs run under
-//               this epilogue. (Stored straight from the registers, one row per thread, the
-//               16-byte writes of 32 rows per instruction slowed the MMAs sharing the SM's
-//               load/store path: 2.14 vs 2.01 ms at 32768 x 15360 x 5120.)
+//               (two 4 KB slices per warp) and written by TMA tensor stores, or, when the
+//               output also goes to other GPUs or an int32 copy is asked for, by the warp with
+//               each store instruction covering four 128-byte row segments; double-buffered
+//               accumulators let the next tile's MMAs run under this epilogue. (Stored
+//               straight from the registers, one row per thread, the 16-byte writes of 32 rows
+//               per instruction slowed the MMAs sharing the SM's load/store path: 2.14 vs 2.01
+//               ms at 32768 x 15360 x 5120.)
 // Every mbarrier wait is bounded (slim_ptx.cuh); on a timeout the kernel records an error,
 // drains its own TMA loads and MMAs, frees TMEM and returns.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <cstring>
 
 #include "slim_kernels.h"
 #include "slim_ptx.cuh"
@@ -48,7 +51,8 @@ constexpr int MMA_K = 32;
 constexpr uint32_t IDESC = idesc_i8(BM, BN);
 
 constexpr int EPI_WARPS = 4;
-constexpr int STAGING_BYTES = 32 * 128;  // per epilogue warp: 32 rows x 64 bf16
+constexpr int SLICE_BYTES = 32 * 128;       // one write-back slice: 32 rows x 64 bf16
+constexpr int STAGING_BYTES = 2 * SLICE_BYTES;  // per epilogue warp: two slices in flight
 
 struct Shared {
   uint64_t full[STAGES];
@@ -153,11 +157,41 @@ __device__ __forceinline__ void store_rows_staged(__nv_bfloat16* out, void* cons
   __syncwarp();  // the staging rows are read before the next slice overwrites them
 }
 
+// The same slice written by a TMA tensor store (box ROW_BYTES/2 columns x 32 rows, swizzle
+// matching the staging layout: 32/64/128-byte swizzle for 32/64/128-byte rows). The warp's two
+// staging slices alternate; lane 0 issues the store and, before a slice is refilled, waits until
+// the store issued from it two slices earlier has read it. Rows >= M and columns >= N fall
+// outside the tensor map and are not written.
 template <int ROW_BYTES>
-__device__ __forceinline__ void store_slice(const GemmI8Params& p, uint8_t* stg, const uint32_t* w, int64_t m0,
-                                            int64_t n0, int lane) {
-  store_rows_staged<ROW_BYTES>(static_cast<__nv_bfloat16*>(p.out), p.peer_out, p.n_peer, p.ldo, p.M, p.N, stg, w, m0,
-                               n0, lane);
+__device__ __forceinline__ void tma_store_slice(const CUtensorMap* tmo, uint8_t* stg, const uint32_t* w, int64_t m0,
+                                                int64_t n0, int lane, uint32_t& slice) {
+  constexpr int CH = ROW_BYTES / 16;
+  auto swz = [](int r) { return (r / (8 / CH)) % CH; };
+  uint8_t* buf = stg + (slice & 1u) * SLICE_BYTES;
+  if (lane == 0) bulk_wait_group_read<1>();
+  __syncwarp();
+  uint4* srow = reinterpret_cast<uint4*>(buf + lane * ROW_BYTES);
+#pragma unroll
+  for (int j = 0; j < CH; ++j) srow[j ^ swz(lane)] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+  fence_proxy_async_smem();  // the rows, written through the generic proxy, are read by TMA
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmo, buf, static_cast<int32_t>(n0), static_cast<int32_t>(m0));
+    bulk_commit_group();
+  }
+  ++slice;
+}
+
+// One slice through TMA when a tensor map is given, else through the warp's own stores.
+template <int ROW_BYTES>
+__device__ __forceinline__ void store_slice(const GemmI8Params& p, const CUtensorMap* tmo, uint8_t* stg,
+                                            const uint32_t* w, int64_t m0, int64_t n0, int lane, uint32_t& slice) {
+  if (tmo != nullptr) {
+    if (m0 < p.M) tma_store_slice<ROW_BYTES>(tmo, stg, w, m0, n0, lane, slice);  // no box starts past the end
+  } else {
+    store_rows_staged<ROW_BYTES>(static_cast<__nv_bfloat16*>(p.out), p.peer_out, p.n_peer, p.ldo, p.M, p.N, stg, w,
+                                 m0, n0, lane);
+  }
 }
 
 // SwiGLU epilogue: the weight rows are interleaved per 256-row tile (128 "up" rows, then the 128
@@ -165,7 +199,8 @@ __device__ __forceinline__ void store_slice(const GemmI8Params& p, uint8_t* stg,
 // column n_base/2 + i gets bf16(up * bf16(silu(gate))), with up and gate the bf16 linear
 // outputs: the roundings of running the linear in bf16 and then ComfyUI's swiglu on its output.
 __device__ __forceinline__ void epilogue_rows_swiglu(const GemmI8Params& p, uint32_t tbase, int64_t m0, int lane,
-                                                     float sam, int64_t n_base, uint8_t* stg) {
+                                                     float sam, int64_t n_base, uint8_t* stg, const CUtensorMap* tmo,
+                                                     uint32_t& slice) {
   const int64_t o_base = n_base / 2;
 #pragma unroll 1
   for (int c = 0; c < BN / 64; ++c) {
@@ -190,18 +225,19 @@ __device__ __forceinline__ void epilogue_rows_swiglu(const GemmI8Params& p, uint
 #pragma unroll
       for (int e = 0; e < 4; ++e) w[j / 2 + e] = pack_bf16x2(y[2 * e], y[2 * e + 1]);
     }
-    store_slice<64>(p, stg, w, m0, o_base + c * 32, lane);
+    store_slice<64>(p, tmo, stg, w, m0, o_base + c * 32, lane, slice);
   }
 }
 
 // One accumulator tile row-slice: this thread's row m0 + lane (TMEM lane), 256 columns from
 // n_base, read 64 columns at a time; scale/bias(/GELU) in fp32, bf16 rows written back through
-// the warp's staging buffer `stg`, optional int32 copy. All 32 lanes of the warp must call it
-// (tcgen05.ld is warp-collective).
+// the warp's staging buffer `stg` (by TMA when `tmo` is given), optional int32 copy. All 32
+// lanes of the warp must call it (tcgen05.ld is warp-collective).
 __device__ __forceinline__ void epilogue_rows(const GemmI8Params& p, uint32_t tbase, int64_t m0, int lane,
-                                              bool row_ok, float sam, int64_t n_base, uint8_t* stg) {
+                                              bool row_ok, float sam, int64_t n_base, uint8_t* stg,
+                                              const CUtensorMap* tmo, uint32_t& slice) {
   if (p.epilogue == kEpiSwiGLU) {
-    epilogue_rows_swiglu(p, tbase, m0, lane, sam, n_base, stg);
+    epilogue_rows_swiglu(p, tbase, m0, lane, sam, n_base, stg, tmo, slice);
     return;
   }
   const int64_t m = m0 + lane;
@@ -254,13 +290,14 @@ __device__ __forceinline__ void epilogue_rows(const GemmI8Params& p, uint32_t tb
 #pragma unroll
       for (int e = 0; e < 4; ++e) w[j / 2 + e] = pack_bf16x2(y[2 * e], y[2 * e + 1]);
     }
-    store_slice<128>(p, stg, w, m0, n0, lane);
+    store_slice<128>(p, tmo, stg, w, m0, n0, lane, slice);
   }
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_i8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-               const GemmI8Params p, int tiles_m, int tiles_n) {
+               const __grid_constant__ CUtensorMap tma_o, const GemmI8Params p, int tiles_m, int tiles_n,
+               int tma_store) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
@@ -378,6 +415,8 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
   } else {
     // epilogue warps 2..5
     const int quarter = warp & 3;
+    const CUtensorMap* tmo = tma_store ? &tma_o : nullptr;
+    uint32_t slice = 0;
     int as = 0;
     uint32_t aphase = 0;
     for (int64_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
@@ -396,12 +435,13 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(as * BN);
       epilogue_rows(p, tbase, m0, lane, row_ok, sam, static_cast<int64_t>(tn) * BN,
-                    staging + (warp - 2) * STAGING_BYTES);
+                    staging + (warp - 2) * STAGING_BYTES, tmo, slice);
       tc_fence_before();
       mbar_arrive(&sh.tempty[as]);
       as ^= 1;
       if (as == 0) aphase ^= 1;
     }
+    if (lane == 0) bulk_wait_group<0>();  // the tensor stores are complete before the CTA exits
   }
 
   tc_fence_before();
@@ -459,7 +499,8 @@ __device__ __forceinline__ void tile_coords2(int64_t t, int tiles_m, int tiles_n
 // tiles_m counts 256-row tiles, tiles_n 256-column tiles.
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                    const GemmI8Params p, int tiles_m, int tiles_n) {
+                    const __grid_constant__ CUtensorMap tma_o, const GemmI8Params p, int tiles_m, int tiles_n,
+                    int tma_store) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
@@ -588,6 +629,8 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
     __syncwarp();
   } else {
     const int quarter = warp & 3;
+    const CUtensorMap* tmo = tma_store ? &tma_o : nullptr;
+    uint32_t slice = 0;
     int as = 0;
     uint32_t aphase = 0;
     for (int64_t t = pair_id; t < total_tiles; t += npairs) {
@@ -606,12 +649,13 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(as * BN);
       epilogue_rows(p, tbase, m0, lane, row_ok, sam, static_cast<int64_t>(tn) * BN,
-                    staging + (warp - 2) * STAGING_BYTES);
+                    staging + (warp - 2) * STAGING_BYTES, tmo, slice);
       tc_fence_before();
       mbar_arrive_cluster(mapa_shared(smem_u32(&sh.tempty[as]), 0));
       as ^= 1;
       if (as == 0) aphase ^= 1;
     }
+    if (lane == 0) bulk_wait_group<0>();  // the tensor stores are complete before the CTA exits
   }
 
   tc_fence_before();
@@ -658,14 +702,36 @@ static bool make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int
   return r == CUDA_SUCCESS;
 }
 
+// Output map for the epilogue's tensor stores: bf16 [M, cols] with row pitch ldo, boxes of
+// 32 rows x (64 columns, 128-byte swizzle) or, for the half-width SwiGLU output, (32 columns,
+// 64-byte swizzle): the staging layouts of tma_store_slice.
+static bool make_out_map(CUtensorMap* map, void* out, int64_t M, int64_t cols, int64_t ldo, bool half_width) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(M)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldo) * 2};
+  const cuuint32_t box[2] = {half_width ? 32u : 64u, 32u};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         half_width ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 cudaError_t launch_gemm_i8(const GemmI8Params& p, cudaStream_t st) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const bool use_pair = p.M > gi8::BM;
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, mo;
   if (!make_kmajor_map(&ma, p.a, p.M, p.K, gi8::BM)) return cudaErrorInvalidValue;
   if (!make_kmajor_map(&mb, p.b, p.N, p.K, use_pair ? gi8::pair::BNH : gi8::BN)) return cudaErrorInvalidValue;
+  // tensor stores unless the tile also goes to other GPUs or to the int32 copy
+  const bool half = p.epilogue == kEpiSwiGLU;
+  const int tma_store = p.n_peer == 0 && p.acc_dbg == nullptr && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
+                        p.ldo % 8 == 0 && make_out_map(&mo, p.out, p.M, half ? p.N / 2 : p.N, p.ldo, half);
+  if (!tma_store) memset(&mo, 0, sizeof(mo));
   const int tiles_n = static_cast<int>((p.N + gi8::BN - 1) / gi8::BN);
   if (use_pair) {
     const int tiles_m = static_cast<int>((p.M + 2 * gi8::BM - 1) / (2 * gi8::BM));
@@ -696,7 +762,8 @@ cudaError_t launch_gemm_i8(const GemmI8Params& p, cudaStream_t st) {
     }
     const int64_t total = static_cast<int64_t>(tiles_m) * tiles_n;
     const int pairs = static_cast<int>(total < max_pairs[dev] ? total : max_pairs[dev]);
-    gi8::pair::gemm_i8_pair_kernel<<<2 * pairs, gi8::THREADS, gi8::pair::SMEM_BYTES, st>>>(ma, mb, p, tiles_m, tiles_n);
+    gi8::pair::gemm_i8_pair_kernel<<<2 * pairs, gi8::THREADS, gi8::pair::SMEM_BYTES, st>>>(ma, mb, mo, p, tiles_m,
+                                                                                           tiles_n, tma_store);
     return cudaGetLastError();
   }
   const int tiles_m = static_cast<int>((p.M + gi8::BM - 1) / gi8::BM);
@@ -709,7 +776,7 @@ cudaError_t launch_gemm_i8(const GemmI8Params& p, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     attr_set1[dev] = true;
   }
-  gi8::gemm_i8_kernel<<<grid, gi8::THREADS, gi8::SMEM_BYTES, st>>>(ma, mb, p, tiles_m, tiles_n);
+  gi8::gemm_i8_kernel<<<grid, gi8::THREADS, gi8::SMEM_BYTES, st>>>(ma, mb, mo, p, tiles_m, tiles_n, tma_store);
   return cudaGetLastError();
 }
 
