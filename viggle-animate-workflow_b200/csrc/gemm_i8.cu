@@ -158,17 +158,17 @@ __device__ __forceinline__ void store_rows_staged(__nv_bfloat16* out, void* cons
 }
 
 // The same slice written by a TMA tensor store (box ROW_BYTES/2 columns x 32 rows, swizzle
-// matching the staging layout: 32/64/128-byte swizzle for 32/64/128-byte rows). The warp's two
-// staging slices alternate; lane 0 issues the store and, before a slice is refilled, waits until
-// the store issued from it two slices earlier has read it. Rows >= M and columns >= N fall
-// outside the tensor map and are not written.
-template <int ROW_BYTES>
+// matching the staging layout: 32/64/128-byte swizzle for 32/64/128-byte rows). The warp's NBUF
+// staging slices of 32 x ROW_BYTES bytes take turns; lane 0 issues the store and, before a slice
+// is refilled, waits until the store issued from it NBUF slices earlier has read it. Rows >= M
+// and columns >= N fall outside the tensor map and are not written; m0 must be < M.
+template <int ROW_BYTES, int NBUF = 2>
 __device__ __forceinline__ void tma_store_slice(const CUtensorMap* tmo, uint8_t* stg, const uint32_t* w, int64_t m0,
                                                 int64_t n0, int lane, uint32_t& slice) {
   constexpr int CH = ROW_BYTES / 16;
   auto swz = [](int r) { return (r / (8 / CH)) % CH; };
-  uint8_t* buf = stg + (slice & 1u) * SLICE_BYTES;
-  if (lane == 0) bulk_wait_group_read<1>();
+  uint8_t* buf = stg + (slice % NBUF) * (32 * ROW_BYTES);
+  if (lane == 0) bulk_wait_group_read<NBUF - 1>();
   __syncwarp();
   uint4* srow = reinterpret_cast<uint4*>(buf + lane * ROW_BYTES);
 #pragma unroll

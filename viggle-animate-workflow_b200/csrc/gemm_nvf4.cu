@@ -29,10 +29,11 @@
 //   warps 6..13  epilogue: each warp reads 128 accumulator columns of its lane quarter,
 //                scales + biases them (GELU if asked) and packs bf16 in registers, releases the
 //                accumulator to the next tile's MMAs, then writes its 32 rows back through a
-//                1 KB shared-memory buffer, 16 columns at a time, each store instruction
-//                covering 16 rows x 32 bytes. (One row per thread, the 16-byte stores into 32
-//                rows per instruction slowed the MMAs by ~12 %; the ring leaves no room for a
-//                wider buffer, and moving the scale atoms out of the ring to make room put
+//                1 KB shared-memory buffer, 16 columns at a time, by TMA tensor stores (or, for
+//                an output the tensor map cannot describe, with each store instruction of the
+//                warp covering 16 rows x 32 bytes). (One row per thread, the 16-byte stores into
+//                32 rows per instruction slowed the MMAs by ~12 %; the ring leaves no room for
+//                a wider buffer, and moving the scale atoms out of the ring to make room put
 //                their global-memory latency in front of the MMAs.)
 // Every mbarrier wait is bounded; on a timeout the kernel records an error, drains its
 // copies and MMAs, frees TMEM and returns.
@@ -97,7 +98,8 @@ __device__ __forceinline__ void tile_coords(int64_t t, int tiles_m, int tiles_n,
 
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_nvf4_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                 const GemmNvf4Params p, int tiles_m, int tiles_n) {
+                 const __grid_constant__ CUtensorMap tma_o, const GemmNvf4Params p, int tiles_m, int tiles_n,
+                 int tma_store) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
@@ -274,7 +276,7 @@ gemm_nvf4_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     const __nv_bfloat16* bias = static_cast<const __nv_bfloat16*>(p.bias);
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
     const float sb = __ldg(p.sb);
-    uint32_t aphase = 0;
+    uint32_t aphase = 0, slice = 0;
     for (int64_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       bool ok = mbar_wait(&sh.tfull, aphase, kErrWaitTimeoutEpilogue);
       ok = __all_sync(0xffffffffu, ok) && !sh.abort;
@@ -328,15 +330,21 @@ gemm_nvf4_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
       tc_fence_before();
       mbar_arrive(&sh.tempty);  // the accumulator is in registers: the next tile may start
       aphase ^= 1;
-      if (cols_ok) {  // warp-uniform
-        const int64_t m0 = static_cast<int64_t>(tm) * BM + quarter * 32;
+      const int64_t m0 = static_cast<int64_t>(tm) * BM + quarter * 32;
+      if (cols_ok && m0 < p.M) {  // warp-uniform
         uint8_t* stg = staging + (warp - EPI_WARP0) * STAGING_BYTES;
 #pragma unroll
-        for (int c = 0; c < 256 / EPI_ROW_BYTES; ++c)
-          gi8::store_rows_staged<EPI_ROW_BYTES>(out, nullptr, 0, p.ldo, p.M, p.N, stg, pk + c * (EPI_ROW_BYTES / 4), m0,
-                                                nbase + c * (EPI_ROW_BYTES / 2), lane);
+        for (int c = 0; c < 256 / EPI_ROW_BYTES; ++c) {
+          if (tma_store)
+            gi8::tma_store_slice<EPI_ROW_BYTES, 1>(&tma_o, stg, pk + c * (EPI_ROW_BYTES / 4), m0,
+                                                   nbase + c * (EPI_ROW_BYTES / 2), lane, slice);
+          else
+            gi8::store_rows_staged<EPI_ROW_BYTES>(out, nullptr, 0, p.ldo, p.M, p.N, stg, pk + c * (EPI_ROW_BYTES / 4),
+                                                  m0, nbase + c * (EPI_ROW_BYTES / 2), lane);
+        }
       }
     }
+    if (lane == 0) bulk_wait_group<0>();  // the tensor stores are complete before the CTA exits
   }
 
   tc_fence_before();
@@ -356,6 +364,21 @@ cudaError_t launch_gemm_nvf4(const GemmNvf4Params& p, cudaStream_t st) {
   CUtensorMap ma, mb;
   if (!make_kmajor_map(&ma, p.a, p.M, p.K / 2, gf4::BM)) return cudaErrorInvalidValue;
   if (!make_kmajor_map(&mb, p.b, p.N, p.K / 2, gf4::BN)) return cudaErrorInvalidValue;
+  // output map for the epilogue's tensor stores: boxes of 32 rows x 16 columns, 32-byte swizzle
+  CUtensorMap mo;
+  int tma_store = 0;
+  if ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && p.ldo % 8 == 0) {
+    PFN_encodeTiled enc = get_encode_fn();
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.N), static_cast<cuuint64_t>(p.M)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.ldo) * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(gf4::EPI_ROW_BYTES / 2), 32u};
+    const cuuint32_t estr[2] = {1, 1};
+    tma_store = enc != nullptr &&
+                enc(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.out, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
+  if (!tma_store) memset(&mo, 0, sizeof(mo));
   const int tiles_m = static_cast<int>((p.M + gf4::BM - 1) / gf4::BM);
   const int tiles_n = static_cast<int>((p.N + gf4::BN - 1) / gf4::BN);
   const int64_t total = static_cast<int64_t>(tiles_m) * tiles_n;
@@ -367,7 +390,7 @@ cudaError_t launch_gemm_nvf4(const GemmNvf4Params& p, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  gf4::gemm_nvf4_kernel<<<grid, gf4::THREADS, gf4::SMEM_BYTES, st>>>(ma, mb, p, tiles_m, tiles_n);
+  gf4::gemm_nvf4_kernel<<<grid, gf4::THREADS, gf4::SMEM_BYTES, st>>>(ma, mb, mo, p, tiles_m, tiles_n, tma_store);
   return cudaGetLastError();
 }
 
