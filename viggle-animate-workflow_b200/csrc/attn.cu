@@ -481,14 +481,20 @@ flash_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
       const float4* ks4 = reinterpret_cast<const float4*>(sKS + s * KS_BYTES) + half * 16;
       const int64_t left = p.seq - static_cast<int64_t>(j) * BN - half * 64;
       const int valid = left < 64 ? static_cast<int>(left) : 64;
+      // y = float(s) * ks in packed pairs: the biased integer read as a float minus 1.5 * 2^23
+      // (exact, see i2f_exact), then the key scale, each lane rounded as the scalar code
       float y[64];
+      const float2 unbias = make_float2(-12582912.0f, -12582912.0f);
 #pragma unroll
       for (int c = 0; c < 64; c += 4) {
         const float4 k4 = ks4[c / 4];
-        y[c + 0] = __fmul_rn(i2f_exact(sr[c + 0]), k4.x);
-        y[c + 1] = __fmul_rn(i2f_exact(sr[c + 1]), k4.y);
-        y[c + 2] = __fmul_rn(i2f_exact(sr[c + 2]), k4.z);
-        y[c + 3] = __fmul_rn(i2f_exact(sr[c + 3]), k4.w);
+        const float2 f0 = add2(make_float2(__uint_as_float(sr[c + 0] + 0x4B400000u),
+                                           __uint_as_float(sr[c + 1] + 0x4B400000u)), unbias);
+        const float2 f1 = add2(make_float2(__uint_as_float(sr[c + 2] + 0x4B400000u),
+                                           __uint_as_float(sr[c + 3] + 0x4B400000u)), unbias);
+        const float2 y0 = mul2(f0, make_float2(k4.x, k4.y));
+        const float2 y1 = mul2(f1, make_float2(k4.z, k4.w));
+        y[c + 0] = y0.x; y[c + 1] = y0.y; y[c + 2] = y1.x; y[c + 3] = y1.y;
       }
       if (valid < 64) {
 #pragma unroll
@@ -535,15 +541,16 @@ flash_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         break;
       }
       uint8_t* prow = sP + b * P_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
-      const float nm = -m_new;
+      const float2 ra2 = make_float2(ra, ra), nm2 = make_float2(-m_new, -m_new);
 #pragma unroll
       for (int c16 = 0; c16 < 4; ++c16) {
         uint32_t w[4];
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           const int c = c16 * 16 + q4 * 4;
-          w[q4] = f32x4_to_e4m3x4(ex2_approx(__fmaf_rn(y[c + 0], ra, nm)), ex2_approx(__fmaf_rn(y[c + 1], ra, nm)),
-                                  ex2_approx(__fmaf_rn(y[c + 2], ra, nm)), ex2_approx(__fmaf_rn(y[c + 3], ra, nm)));
+          const float2 e0 = fma2(make_float2(y[c + 0], y[c + 1]), ra2, nm2);  // y * ra - m', rounded once
+          const float2 e1 = fma2(make_float2(y[c + 2], y[c + 3]), ra2, nm2);
+          w[q4] = f32x4_to_e4m3x4(ex2_approx(e0.x), ex2_approx(e0.y), ex2_approx(e1.x), ex2_approx(e1.y));
         }
         const int chunk = half * 4 + c16;
         *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
