@@ -266,3 +266,54 @@ def test_ffn_c_entry_equals_two_linears(cuda, act, lead):
     assert rc != 0
     with pytest.raises(ValueError):
         ops.ffn_int8(xt, qdd, sdd, qud, sud)
+
+
+_THREADS_SCRIPT = r"""
+import sys, threading
+sys.path[:0] = sys.argv[1:]
+import numpy as np, torch
+import synthetic
+from slimdit import ops, attention, _native
+dev = torch.device("cuda", 0)
+torch.cuda.set_device(dev)
+qw, sw = ops.rotate_quant(torch.from_numpy(synthetic.weight(512, 1024, seed=1)).to(dev).to(torch.bfloat16))
+xs = [torch.from_numpy(synthetic.activations(64 + 97 * i, 1024, seed=i)).to(dev).to(torch.bfloat16) for i in range(8)]
+qkv = (torch.randn((300, 3 * 2 * 128), generator=torch.Generator().manual_seed(3)) * 0.5).to(torch.bfloat16).to(dev)
+torch.cuda.synchronize()
+outs, errors = [None] * 8, []
+start = threading.Barrier(8)
+def work(i):
+    try:
+        s = torch.cuda.Stream(device=dev)
+        start.wait()  # the first library calls of the process, all at once
+        with torch.cuda.stream(s):
+            y = ops.int8_linear(xs[i], qw, sw)
+            a = attention.attention_packed(qkv, 2) if i % 2 else None
+        s.synchronize()
+        outs[i] = (y, a)
+    except Exception as exc:  # reported below
+        errors.append(repr(exc))
+threads = [threading.Thread(target=work, args=(i,)) for i in range(8)]
+[t.start() for t in threads]
+[t.join() for t in threads]
+assert not errors, errors
+for i in range(8):
+    assert torch.equal(outs[i][0], ops.int8_linear(xs[i], qw, sw)), i
+    if i % 2:
+        assert torch.equal(outs[i][1], attention.attention_packed(qkv, 2)), i
+assert _native.device_error() == 0
+print("threads ok")
+"""
+
+
+def test_first_calls_from_many_threads_at_once(cuda):
+    """Eight host threads, each on its own stream, make the process's first library calls at the
+    same moment (the lazy per-device caches race for real only then): every result equals the
+    one a single thread gets afterwards."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    paths = [str(root / "viggle-animate-workflow_b200"), str(root), str(root / "tests")]
+    r = subprocess.run([sys.executable, "-c", _THREADS_SCRIPT, *paths], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "threads ok" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]

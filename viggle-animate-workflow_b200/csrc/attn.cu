@@ -280,12 +280,6 @@ struct Params {
   float attn_scale;
 };
 
-// int32 -> fp32 for |s| < 2^22 without the conversion unit: the bits of s + 1.5 * 2^23 read as a
-// float are exactly 1.5 * 2^23 + s. Exact for every score (|s| <= 128 * 127 * 127 < 2^21).
-__device__ __forceinline__ float i2f_exact(uint32_t s) {
-  return __fsub_rn(__uint_as_float(s + 0x4B400000u), 12582912.0f);
-}
-
 __device__ __forceinline__ uint32_t f32x4_to_e4m3x4(float a, float b, float c, float d) {
   const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
   const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
@@ -481,8 +475,10 @@ flash_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
       const float4* ks4 = reinterpret_cast<const float4*>(sKS + s * KS_BYTES) + half * 16;
       const int64_t left = p.seq - static_cast<int64_t>(j) * BN - half * 64;
       const int valid = left < 64 ? static_cast<int>(left) : 64;
-      // y = float(s) * ks in packed pairs: the biased integer read as a float minus 1.5 * 2^23
-      // (exact, see i2f_exact), then the key scale, each lane rounded as the scalar code
+      // y = float(s) * ks in packed pairs. int32 -> fp32 without the conversion unit: the bits of
+      // s + 1.5 * 2^23 read as a float are exactly 1.5 * 2^23 + s for |s| < 2^22 (every score:
+      // |s| <= 128 * 127 * 127 < 2^21), so subtracting 1.5 * 2^23 is exact; then the key scale,
+      // each lane rounded as the scalar code would be
       float y[64];
       const float2 unbias = make_float2(-12582912.0f, -12582912.0f);
 #pragma unroll
@@ -667,14 +663,14 @@ typedef CUresult (*PFN_encodeTiledAttn)(CUtensorMap*, CUtensorMapDataType, cuuin
                                         CUtensorMapFloatOOBfill);
 
 static PFN_encodeTiledAttn attn_encode_fn() {
-  static PFN_encodeTiledAttn fn = nullptr;
-  if (fn == nullptr) {
+  static const PFN_encodeTiledAttn fn = []() -> PFN_encodeTiledAttn {  // looked up once, thread-safe
     void* sym = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &sym, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_encodeTiledAttn>(sym);
-  }
+      return reinterpret_cast<PFN_encodeTiledAttn>(sym);
+    return nullptr;
+  }();
   return fn;
 }
 
@@ -742,13 +738,12 @@ cudaError_t launch_attn_flash(const int8_t* q, const float* qs_t, const int8_t* 
     return cudaErrorInvalidValue;
   int dev = 0;
   cudaGetDevice(&dev);
-  static bool attr_set[64] = {false};
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(F::flash_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(F::SMEM_BYTES));
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+  static PerDeviceOnce smem_once;
+  const cudaError_t e = smem_once.run(dev, [] {
+    return cudaFuncSetAttribute(F::flash_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(F::SMEM_BYTES));
+  });
+  if (e != cudaSuccess) return e;
   F::Params p{qs_t, ks_t, v_amax, static_cast<__nv_bfloat16*>(out), ldo, seq, seq_pad, attn_scale};
   const dim3 grid(static_cast<unsigned>((seq + F::BM - 1) / F::BM), static_cast<unsigned>(heads));
   F::flash_kernel<<<grid, F::THREADS, F::SMEM_BYTES, st>>>(mq, mk, mv, p);

@@ -677,14 +677,14 @@ typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_
                                     CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 static PFN_encodeTiled get_encode_fn() {
-  static PFN_encodeTiled fn = nullptr;
-  if (fn == nullptr) {
+  static const PFN_encodeTiled fn = []() -> PFN_encodeTiled {  // looked up once, thread-safe
     void* sym = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &sym, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_encodeTiled>(sym);
-  }
+      return reinterpret_cast<PFN_encodeTiled>(sym);
+    return nullptr;
+  }();
   return fn;
 }
 
@@ -735,15 +735,15 @@ cudaError_t launch_gemm_i8(const GemmI8Params& p, cudaStream_t st) {
   const int tiles_n = static_cast<int>((p.N + gi8::BN - 1) / gi8::BN);
   if (use_pair) {
     const int tiles_m = static_cast<int>((p.M + 2 * gi8::BM - 1) / (2 * gi8::BM));
-    static bool attr_set[64] = {false};
-    if (dev < 64 && !attr_set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(gi8::pair::gemm_i8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(gi8::pair::SMEM_BYTES));
-      if (e != cudaSuccess) return e;
-      attr_set[dev] = true;
-    }
-    static int max_pairs[64] = {0};
-    if (dev < 64 && max_pairs[dev] == 0) {
+    static PerDeviceOnce smem_once, pairs_once;
+    cudaError_t e = smem_once.run(dev, [] {
+      return cudaFuncSetAttribute(gi8::pair::gemm_i8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(gi8::pair::SMEM_BYTES));
+    });
+    if (e != cudaSuccess) return e;
+    static int max_pairs[64] = {0};  // clusters of 2 that fit at once, per device
+    int cap = sms / 2;
+    pairs_once.run(dev, [&] {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * (sms / 2));
       cfg.blockDim = dim3(gi8::THREADS);
@@ -758,10 +758,13 @@ cudaError_t launch_gemm_i8(const GemmI8Params& p, cudaStream_t st) {
       int clusters = 0;
       if (cudaOccupancyMaxActiveClusters(&clusters, gi8::pair::gemm_i8_pair_kernel, &cfg) != cudaSuccess || clusters < 1)
         clusters = sms / 2;
-      max_pairs[dev] = clusters;
-    }
+      if (dev >= 0 && dev < 64) max_pairs[dev] = clusters;
+      cap = clusters;
+      return cudaSuccess;
+    });
+    if (dev >= 0 && dev < 64) cap = max_pairs[dev];
     const int64_t total = static_cast<int64_t>(tiles_m) * tiles_n;
-    const int pairs = static_cast<int>(total < max_pairs[dev] ? total : max_pairs[dev]);
+    const int pairs = static_cast<int>(total < cap ? total : cap);
     gi8::pair::gemm_i8_pair_kernel<<<2 * pairs, gi8::THREADS, gi8::pair::SMEM_BYTES, st>>>(ma, mb, mo, p, tiles_m,
                                                                                            tiles_n, tma_store);
     return cudaGetLastError();
@@ -769,13 +772,12 @@ cudaError_t launch_gemm_i8(const GemmI8Params& p, cudaStream_t st) {
   const int tiles_m = static_cast<int>((p.M + gi8::BM - 1) / gi8::BM);
   const int64_t total = static_cast<int64_t>(tiles_m) * tiles_n;
   const int grid = static_cast<int>(total < sms ? total : sms);
-  static bool attr_set1[64] = {false};
-  if (dev < 64 && !attr_set1[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gi8::gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(gi8::SMEM_BYTES));
-    if (e != cudaSuccess) return e;
-    attr_set1[dev] = true;
-  }
+  static PerDeviceOnce smem_once1;
+  const cudaError_t e = smem_once1.run(dev, [] {
+    return cudaFuncSetAttribute(gi8::gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(gi8::SMEM_BYTES));
+  });
+  if (e != cudaSuccess) return e;
   gi8::gemm_i8_kernel<<<grid, gi8::THREADS, gi8::SMEM_BYTES, st>>>(ma, mb, mo, p, tiles_m, tiles_n, tma_store);
   return cudaGetLastError();
 }

@@ -383,13 +383,12 @@ cudaError_t launch_gemm_nvf4(const GemmNvf4Params& p, cudaStream_t st) {
   const int tiles_n = static_cast<int>((p.N + gf4::BN - 1) / gf4::BN);
   const int64_t total = static_cast<int64_t>(tiles_m) * tiles_n;
   const int grid = static_cast<int>(total < sms ? total : sms);
-  static bool attr_set[64] = {false};
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gf4::gemm_nvf4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(gf4::SMEM_BYTES));
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+  static PerDeviceOnce smem_once;
+  const cudaError_t e = smem_once.run(dev, [] {
+    return cudaFuncSetAttribute(gf4::gemm_nvf4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(gf4::SMEM_BYTES));
+  });
+  if (e != cudaSuccess) return e;
   gf4::gemm_nvf4_kernel<<<grid, gf4::THREADS, gf4::SMEM_BYTES, st>>>(ma, mb, mo, p, tiles_m, tiles_n, tma_store);
   return cudaGetLastError();
 }
