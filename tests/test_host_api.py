@@ -104,6 +104,29 @@ def test_abi_validation_errors_need_no_device():
     assert "group_size" in _native.last_error() or _native.last_error() != ""
 
 
+def test_ffn_and_attention_entries_validate_before_any_device_work():
+    """slim_ffn_i8 takes only an FFN activation and sane sizes; the attention entries take only
+    head dim 128. Both reject the rest with a code and a message, with no CUDA call made."""
+    from slimdit import _native
+    lib = _native.load()
+    d = ctypes.c_void_p(16)
+
+    def ffn(act, m=4, k=512, f=1024):
+        return lib.slim_ffn_i8(d, _native.BF16, d, d, None, d, d, None, d, d, d, d, d, d, m, k, f, act, None)
+
+    assert ffn(_native.EPI_SCALE_BIAS) == _native.SLIM_ERR_DTYPE
+    assert "activation" in _native.last_error()
+    assert ffn(_native.EPI_GELU_TANH, f=0) == _native.SLIM_ERR_SHAPE
+    assert ffn(_native.EPI_GELU_TANH, k=300) == _native.SLIM_ERR_GROUP
+    assert ffn(_native.EPI_SWIGLU, m=0) == _native.SLIM_OK  # empty: nothing to do
+    b = ctypes.c_uint64(0)
+    assert lib.slim_attn_workspace_bytes(100, 2, 96, ctypes.byref(b)) != _native.SLIM_OK
+    assert lib.slim_attn_workspace_bytes(100, 2, 128, None) == _native.SLIM_ERR_NULL
+    assert lib.slim_attn_workspace_bytes(100, 2, 128, ctypes.byref(b)) == _native.SLIM_OK and b.value > 0
+    assert lib.slim_attn_packed(d, 100, 2, 64, 1, d, d, b.value, None) != _native.SLIM_OK
+    assert lib.slim_attn_packed(None, 100, 2, 128, 1, d, d, b.value, None) == _native.SLIM_ERR_NULL
+
+
 def test_error_mapping_to_python_exceptions():
     from slimdit import _native
     lib = _native.load()
