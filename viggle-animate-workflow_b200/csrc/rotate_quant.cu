@@ -348,6 +348,196 @@ __global__ void __launch_bounds__(256) ref_rotate4_kernel(const void* __restrict
   }
 }
 
+// Reference order for 5 <= G <= 64 with sixteen outputs per thread: thread t of a CTA (one row
+// at a time) takes group t/16 and outputs jl + 16*i, i = 0..15, jl = t%16. With the base-4
+// digits of j (j0, j1 from jl; a = j2 = i%4, c = j3 = i/4) the sign of term k = 16*b + l is
+// lam(l) * sig16(i, b): lam(l) = H4[j1][l/4] * H4[j0][l%4] is the same for the thread's
+// sixteen outputs, so each input loaded from shared memory feeds sixteen fused adds (the
+// four-output kernel loads four times as often per add). Carrying each accumulator as
+// sig16(i, b) * acc, as in ref_rotate_four0, every step is fma(x, lam, acc), and at block b the
+// carried value is multiplied by sig16(i, b) * sig16(i, b-1). Outputs whose multipliers have
+// been equal at every block change so far hold equal carried accumulators, so one chain serves
+// them: rep16(i, b) names the output whose chain output i shares during block b (H4 has -1
+// exactly where the digits sum to 3, which gives one chain in block 0, two in block 1, four in
+// blocks 2-3, eight in 4-7 and sixteen from 8 on: 2,736 fused adds per sixteen outputs instead
+// of 4,096). Each output still sees exactly the operations of its own sequential chain.
+__host__ __device__ constexpr int rep16(int i, int b) {
+  return b == 0 ? 0
+         : b == 1 ? ((i & 3) < 2 ? 0 : 2)
+         : b < 4 ? (i & 3)
+         : b < 8 ? (i & 3) + 4 * ((i >> 2) < 2 ? 0 : 2)
+         : i;
+}
+
+__device__ __forceinline__ float sig16(int i, int b) { return h4sign(i & 3, b & 3) * h4sign(i >> 2, b >> 2); }
+
+// Compile-time twins of h4sign / sig16 for the per-block template below.
+__host__ __device__ constexpr float h4c(int a, int b) { return (a + b == 3) ? -1.0f : 1.0f; }
+__host__ __device__ constexpr float sig16c(int i, int b) { return h4c(i & 3, b & 3) * h4c(i >> 2, b >> 2); }
+
+// Block B of the sixteen carried chains: the class split / sign change at entry, then sixteen
+// steps, pairs (2p, 2p+1) that are both chains advancing with one packed fp32x2 fma.
+template <int B>
+__device__ __forceinline__ void chain16_block(const float4* __restrict__ x4, const float (&lam)[16],
+                                              float (&acc)[16]) {
+  if constexpr (B > 0) {
+    float old[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) old[i] = acc[i];
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (rep16(i, B) == i) acc[i] = old[rep16(i, B - 1)] * (sig16c(i, B) * sig16c(i, B - 1));
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 v = x4[B * 4 + q];
+    const float xv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lv = lam[4 * q + e];
+#pragma unroll
+      for (int pr = 0; pr < 8; ++pr) {
+        const int i0 = 2 * pr, i1 = 2 * pr + 1;
+        const bool r0 = rep16(i0, B) == i0, r1 = rep16(i1, B) == i1;
+        if (r0 && r1) {
+          const float2 r = fma2(make_float2(xv[e], xv[e]), make_float2(lv, lv), make_float2(acc[i0], acc[i1]));
+          acc[i0] = r.x;
+          acc[i1] = r.y;
+        } else if (r0) {
+          acc[i0] = __fmaf_rn(xv[e], lv, acc[i0]);
+        } else if (r1) {
+          acc[i1] = __fmaf_rn(xv[e], lv, acc[i1]);
+        }
+      }
+    }
+  }
+}
+
+template <int B>
+struct Chain16 {
+  __device__ __forceinline__ static void run(const float4* __restrict__ x4, const float (&lam)[16], float (&acc)[16]) {
+    chain16_block<B>(x4, lam, acc);
+    Chain16<B + 1>::run(x4, lam, acc);
+  }
+};
+template <>
+struct Chain16<16> {
+  __device__ __forceinline__ static void run(const float4*, const float (&)[16], float (&)[16]) {}
+};
+
+// A thread's 16 consecutive inputs of a row (raw words: bf16/f16 2 x 16 B, fp32 4 x 16 B,
+// int8 codes 16 B), loaded one row ahead and written to shared memory as fp32 after the row
+// in flight is done.
+template <int DT, bool DEQ>
+struct Row16 {
+  static constexpr int kWords = DEQ ? 1 : (DT == kF32 ? 4 : 2);
+  uint4 w[kWords];
+  float rs;
+  __device__ __forceinline__ void load(const void* x, const float* deq_scale, int64_t row, int K, int t) {
+    const int64_t e0 = row * static_cast<int64_t>(K) + 16 * t;
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const unsigned char*>(x) +
+                                                     e0 * (DEQ ? 1 : (DT == kF32 ? 4 : 2)));
+#pragma unroll
+    for (int i = 0; i < kWords; ++i) w[i] = __ldg(p + i);
+    rs = DEQ ? __ldg(deq_scale + row) : 1.0f;
+  }
+  __device__ __forceinline__ void store(float* dst) const {
+    float f[16];
+    if (DEQ) {
+      const uint32_t u[4] = {w[0].x, w[0].y, w[0].z, w[0].w};
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        f[i] = static_cast<float>(static_cast<int8_t>((u[i >> 2] >> (8 * (i & 3))) & 0xffu)) * rs;
+    } else if (DT == kF32) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        f[4 * i] = __uint_as_float(w[i].x); f[4 * i + 1] = __uint_as_float(w[i].y);
+        f[4 * i + 2] = __uint_as_float(w[i].z); f[4 * i + 3] = __uint_as_float(w[i].w);
+      }
+    } else {
+      const uint32_t u[8] = {w[0].x, w[0].y, w[0].z, w[0].w, w[1].x, w[1].y, w[1].z, w[1].w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (DT == kBF16) {
+          f[2 * i] = __uint_as_float(u[i] << 16);
+          f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+        } else {
+          const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+          f[2 * i] = h.x; f[2 * i + 1] = h.y;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(f[i], f[i + 1], f[i + 2], f[i + 3]);
+  }
+};
+
+template <int DT, bool DEQ, int MODE>
+__global__ void __launch_bounds__(1024) ref_rotate16_kernel(const void* __restrict__ x,
+                                                           const float* __restrict__ deq_scale,
+                                                           int64_t rows, int K,
+                                                           float* __restrict__ rot_out,
+                                                           int8_t* __restrict__ q_out,
+                                                           float* __restrict__ scale_out) {
+  extern __shared__ __align__(16) float smem_f[];  // two rows of K fp32 inputs
+  __shared__ float red[32];
+  const int t = threadIdx.x;
+  const int g = t >> 4, jl = t & 15;
+  const int groups = K >> 8;
+  const bool active = g < groups;  // whole warps only: the threads past the last group idle
+  float lam[16];
+#pragma unroll
+  for (int l = 0; l < 16; ++l) lam[l] = h4sign(jl >> 2, l >> 2) * h4sign(jl & 3, l & 3);
+  int64_t row = blockIdx.x;
+  if (row >= rows) return;  // uniform over the CTA
+  Row16<DT, DEQ> nxt;
+  if (active) {
+    nxt.load(x, deq_scale, row, K, t);
+    nxt.store(smem_f + 16 * t);
+  }
+  __syncthreads();
+  int buf = 0;
+  for (; row < rows; row += gridDim.x) {
+    const int64_t base = row * static_cast<int64_t>(K);
+    const int64_t next = row + gridDim.x;
+    const bool have_next = next < rows;
+    if (active && have_next) nxt.load(x, deq_scale, next, K, t);  // lands while this row computes
+    const float* xs = smem_f + buf * K;
+    float y[16];
+    float amax = 0.0f;
+    if (active) {
+      const float4* x4 = reinterpret_cast<const float4*>(xs + g * 256);
+      float acc[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
+      Chain16<0>::run(x4, lam, acc);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        y[i] = canon_zero(acc[i] * sig16(i, 15) * 0.0625f);  // the block sign of block 15
+        amax = fmaxf(amax, fabsf(y[i]));
+      }
+    }
+    const int64_t o = base + g * 256 + jl;
+    if (MODE == 0) {
+      if (active) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) rot_out[o + 16 * i] = y[i];
+      }
+    } else {
+      const float m = block_max(amax, red);
+      const float scale = row_scale_from_absmax(m);
+      if (t == 0) scale_out[row] = scale;
+      if (active) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) q_out[o + 16 * i] = quant_code(y[i], scale);
+      }
+    }
+    if (active && have_next) nxt.store(smem_f + (buf ^ 1) * K + 16 * t);
+    __syncthreads();  // the next row is staged; this row's inputs are no longer read
+    buf ^= 1;
+  }
+}
+
 // ------------------------------------------------------------------ butterfly, packed pairs
 // Packed fp32x2 arithmetic: add2 / mul2 / fma2 (slim_ptx.cuh).
 
@@ -616,6 +806,26 @@ static cudaError_t launch_ref(const void* x, const float* deq_scale, int64_t row
                               float* rot_out, int8_t* q, float* scale, cudaStream_t st) {
   const int groups = K >> 8;
   const int kind = groups >= 5 ? 0 : (groups >= 2 ? 1 : 2);
+  // sixteen outputs per thread for rows of up to 64 groups read with 16-byte vector loads (the
+  // four-output kernel takes longer rows and inputs that are not 16-byte aligned)
+  if (kind == 0 && groups <= 64 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+    const int threads = (16 * groups + 31) / 32 * 32;
+    const size_t smem16 = 2 * static_cast<size_t>(K) * sizeof(float);
+    auto fn16 = ref_rotate16_kernel<DT, DEQ, MODE>;
+    static PerDeviceOnce smem_once;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaError_t e = smem_once.run(dev, [&] {
+      return cudaFuncSetAttribute(fn16, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
+    });
+    if (e != cudaSuccess) return e;
+    int per_sm = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn16, threads, smem16);
+    if (e != cudaSuccess) return e;
+    const int grid16 = grid_for_rows(rows, per_sm < 1 ? 1 : per_sm);
+    fn16<<<grid16, threads, smem16, st>>>(x, deq_scale, rows, K, rot_out, q, scale);
+    return cudaGetLastError();
+  }
   if (kind == 0) {
     const size_t smem4 = (1056 + (MODE == 1 ? static_cast<size_t>(K) : 0)) * sizeof(float);
     auto fn4 = ref_rotate4_kernel<DT, DEQ, MODE>;
