@@ -480,7 +480,7 @@ __global__ void __launch_bounds__(1024) ref_rotate16_kernel(const void* __restri
                                                            int8_t* __restrict__ q_out,
                                                            float* __restrict__ scale_out) {
   extern __shared__ __align__(16) float smem_f[];  // two rows of K fp32 inputs
-  __shared__ float red[32];
+  __shared__ float red[2][32];                     // warp maxima, by row parity
   const int t = threadIdx.x;
   const int g = t >> 4, jl = t & 15;
   const int groups = K >> 8;
@@ -518,13 +518,23 @@ __global__ void __launch_bounds__(1024) ref_rotate16_kernel(const void* __restri
       }
     }
     const int64_t o = base + g * 256 + jl;
+    if (MODE == 1) {
+      const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(amax));  // amax >= 0
+      if ((t & 31) == 0) red[buf][t >> 5] = __uint_as_float(wm);
+    }
+    if (active && have_next) nxt.store(smem_f + (buf ^ 1) * K + 16 * t);
+    // one barrier per row: the warp maxima are visible, the next row is staged, and this row's
+    // inputs are no longer read (red[buf] is written again two rows later, after the next one)
+    __syncthreads();
     if (MODE == 0) {
       if (active) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) rot_out[o + 16 * i] = y[i];
       }
     } else {
-      const float m = block_max(amax, red);
+      const int nw = (blockDim.x + 31) >> 5;
+      const int lane = t & 31;
+      const float m = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < nw ? __float_as_uint(red[buf][lane]) : 0u));
       const float scale = row_scale_from_absmax(m);
       if (t == 0) scale_out[row] = scale;
       if (active) {
@@ -532,8 +542,6 @@ __global__ void __launch_bounds__(1024) ref_rotate16_kernel(const void* __restri
         for (int i = 0; i < 16; ++i) q_out[o + 16 * i] = quant_code(y[i], scale);
       }
     }
-    if (active && have_next) nxt.store(smem_f + (buf ^ 1) * K + 16 * t);
-    __syncthreads();  // the next row is staged; this row's inputs are no longer read
     buf ^= 1;
   }
 }
