@@ -55,7 +55,7 @@ def parse_args(argv=None):
     ap.add_argument("--no-secondary", action="store_true", help="skip the FFN and converter measurements")
     ap.add_argument("--secondary-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU work in the cpu_baseline sample")
-    ap.add_argument("--profile-case", choices=["nvfp4", "attn"], default=None,
+    ap.add_argument("--profile-case", choices=["nvfp4", "attn", "rotate"], default=None,
                     help="run only a small case of one workload (for ncu captures; prints no bench line)")
     ap.add_argument("--tokens", type=int, default=16384, help="token rows of the --profile-case run")
     ap.add_argument("--heads", type=int, default=4, help="attention heads of the --profile-case attn run")
@@ -677,6 +677,32 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
 
 
 # ----------------------------------------------------------------------------- profiling cases
+def run_profile_rotate(args) -> int:
+    """The reference-order weight rotation + INT8 of one linear (W bf16 [tokens, 5120], the QKV
+    linear's 15360 rows by default in captures): warm-up + `--steps` calls, for ncu captures."""
+    import torch
+
+    from slimdit import _native, ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    w = (torch.randn((args.tokens, 5120), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    warm = max(1, args.warmup)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(warm + args.steps + 1)]
+    for i in range(warm + args.steps):
+        ev[i].record()
+        ops.rotate_quant(w, order="reference")
+    ev[-1].record()
+    torch.cuda.synchronize(dev)
+    assert _native.device_error() == 0
+    ms = ev[warm].elapsed_time(ev[-1]) / max(1, args.steps)
+    print(json.dumps({"profile_case": "rotate_reference_order", "rows": args.tokens, "K": 5120, "steps": args.steps,
+                      "ms": round(ms, 4)}))
+    return 0
+
+
 def run_profile_attn(args) -> int:
     """A small case of the attention (packed qkv [tokens, 3*heads*128]): the quantisers once,
     then warm-up + `--steps` launches of the flash kernel, for ncu captures."""
@@ -942,6 +968,8 @@ def main(argv=None) -> int:
     args = parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile_case == "rotate":
+        return run_profile_rotate(args)
     if args.profile_case == "attn":
         return run_profile_attn(args)
     if args.profile_case:
