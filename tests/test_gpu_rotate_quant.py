@@ -222,3 +222,18 @@ def test_convrot_beats_the_plain_grid_on_outlier_rows(cuda, k, on_device):
     plain_back = np.clip(np.rint(w / plain_scale), -128, 127) * plain_scale
     plain_err = np.linalg.norm(plain_back - w) / np.linalg.norm(w)
     assert rotated_err < plain_err / 5 and rotated_err < 0.01, (rotated_err, plain_err)
+
+
+def test_dequantize_from_unaligned_codes_matches_aligned(cuda):
+    """slim_dequant_i8 takes int8 codes at any address: codes one byte past an aligned address
+    (read element by element, not with 16-byte vector loads) give the same fp32 bits."""
+    from slimdit import ops
+    n, k = 96, 5120
+    rng = np.random.default_rng(12)
+    q = torch.from_numpy(rng.integers(-128, 128, size=(n, k), dtype=np.int8)).to(cuda)
+    scale = torch.from_numpy((rng.random(n, dtype=np.float32) * 1e-3 + 1e-5).astype(np.float32)).to(cuda)
+    buf = torch.empty(n * k + 1, dtype=torch.int8, device=cuda)
+    shifted = buf[1:].view(n, k)
+    shifted.copy_(q)
+    assert shifted.data_ptr() % 16 != 0
+    assert torch.equal(ops.dequantize(shifted, scale).view(torch.int32), ops.dequantize(q, scale).view(torch.int32))
