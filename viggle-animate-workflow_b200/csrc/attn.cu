@@ -816,6 +816,7 @@ int slim_attn_workspace_bytes(int64_t seq, int heads, int dim, uint64_t* bytes) 
 int slim_attn_quant_qk(const void* qkv, int64_t seq, int heads, int dim, int64_t row_stride, int64_t q_offset,
                        int64_t k_offset, int rotate, int8_t* q, float* q_scale_t, int8_t* k, float* k_scale_t,
                        int64_t seq_pad, void* stream) {
+  SLIM_NVTX("slim_attn_quant_qk");
   int rc;
   if ((rc = attn_shape_checks(seq, heads, dim)) != SLIM_OK) return rc;
   if ((rc = seq_pad_check(seq, seq_pad)) != SLIM_OK) return rc;
@@ -848,6 +849,7 @@ static int attn_v_checks(const void* qkv, int64_t seq, int heads, int dim, int64
 
 int slim_attn_v_amax(const void* qkv, int64_t seq, int heads, int dim, int64_t row_stride, int64_t v_offset,
                      float* v_amax, void* stream) {
+  SLIM_NVTX("slim_attn_v_amax");
   int rc;
   if ((rc = attn_v_checks(qkv, seq, heads, dim, row_stride, v_offset, v_amax)) != SLIM_OK) return rc;
   if (seq == 0) return SLIM_OK;
@@ -860,6 +862,7 @@ int slim_attn_v_amax(const void* qkv, int64_t seq, int heads, int dim, int64_t r
 
 int slim_attn_quant_v_scaled(const void* qkv, int64_t seq, int heads, int dim, int64_t row_stride, int64_t v_offset,
                              uint8_t* v_t, int64_t seq_pad, const float* v_amax, void* stream) {
+  SLIM_NVTX("slim_attn_quant_v_scaled");
   int rc;
   if ((rc = attn_v_checks(qkv, seq, heads, dim, row_stride, v_offset, v_amax)) != SLIM_OK) return rc;
   if ((rc = seq_pad_check(seq, seq_pad)) != SLIM_OK) return rc;
@@ -876,6 +879,7 @@ int slim_attn_quant_v_scaled(const void* qkv, int64_t seq, int heads, int dim, i
 
 int slim_attn_quant_v(const void* qkv, int64_t seq, int heads, int dim, int64_t row_stride, int64_t v_offset,
                       uint8_t* v_t, int64_t seq_pad, float* v_amax, void* stream) {
+  SLIM_NVTX("slim_attn_quant_v");
   int rc;
   if ((rc = attn_shape_checks(seq, heads, dim)) != SLIM_OK) return rc;
   if ((rc = seq_pad_check(seq, seq_pad)) != SLIM_OK) return rc;
@@ -896,6 +900,7 @@ int slim_attn_quant_v(const void* qkv, int64_t seq, int heads, int dim, int64_t 
 int slim_attn_int8(const int8_t* q, const float* q_scale_t, const int8_t* k, const float* k_scale_t,
                    const uint8_t* v_t, const float* v_amax, float attn_scale, int64_t seq, int heads, int dim,
                    int64_t seq_pad, void* out, int64_t ldo, void* stream) {
+  SLIM_NVTX("slim_attn_int8");
   int rc;
   if ((rc = attn_shape_checks(seq, heads, dim)) != SLIM_OK) return rc;
   if ((rc = seq_pad_check(seq, seq_pad)) != SLIM_OK) return rc;
@@ -917,6 +922,7 @@ int slim_attn_int8(const int8_t* q, const float* q_scale_t, const int8_t* k, con
 
 int slim_attn_packed(const void* qkv, int64_t seq, int heads, int dim, int rotate, void* out, void* workspace,
                      uint64_t workspace_bytes, void* stream) {
+  SLIM_NVTX("slim_attn_packed");
   int rc;
   if ((rc = attn_shape_checks(seq, heads, dim)) != SLIM_OK) return rc;
   if (seq == 0) return SLIM_OK;

@@ -101,6 +101,7 @@ int slim_device_error(unsigned int* code) {
 
 int slim_rotate_f32(const void* x, int dtype, int64_t rows, int64_t K, int group, int order,
                     float* out, void* stream) {
+  SLIM_NVTX("slim_rotate_f32");
   int rc;
   if ((rc = check_group(K, group)) != SLIM_OK) return rc;
   if ((rc = check_dtype(dtype)) != SLIM_OK) return rc;
@@ -125,6 +126,7 @@ int slim_rotate_f32(const void* x, int dtype, int64_t rows, int64_t K, int group
 
 int slim_rotate_quant_i8(const void* x, int dtype, int64_t rows, int64_t K, int group, int order,
                          int8_t* q, float* scale, float* rot_out, void* stream) {
+  SLIM_NVTX("slim_rotate_quant_i8");
   int rc;
   if ((rc = check_group(K, group)) != SLIM_OK) return rc;
   if ((rc = check_dtype(dtype)) != SLIM_OK) return rc;
@@ -159,6 +161,7 @@ int slim_rotate_quant_i8(const void* x, int dtype, int64_t rows, int64_t K, int 
 
 int slim_quantize_rows_i8(const float* rotated, int64_t rows, int64_t K, int8_t* q, float* scale,
                           void* stream) {
+  SLIM_NVTX("slim_quantize_rows_i8");
   int rc;
   if (rows < 0 || K <= 0 || K > (int64_t{1} << 30)) return fail(SLIM_ERR_SHAPE, "bad shape [%lld, %lld]", static_cast<long long>(rows), static_cast<long long>(K));
   if (rows == 0) return SLIM_OK;
@@ -172,6 +175,7 @@ int slim_quantize_rows_i8(const float* rotated, int64_t rows, int64_t K, int8_t*
 
 int slim_dequant_i8(const int8_t* q, const float* scale, int64_t rows, int64_t K, int group,
                     float* out, void* stream) {
+  SLIM_NVTX("slim_dequant_i8");
   int rc;
   if ((rc = check_group(K, group)) != SLIM_OK) return rc;
   if (rows < 0) return fail(SLIM_ERR_SHAPE, "negative row count");
@@ -207,6 +211,7 @@ static int gemm_checks(const int8_t* a, const int8_t* b, const float* sa, const 
 
 int slim_gemm_i8(const int8_t* a, const int8_t* b, const float* sa, const float* sb, const void* bias, void* out,
                  int32_t* acc_dbg, int64_t M, int64_t N, int64_t K, int epilogue, void* stream) {
+  SLIM_NVTX("slim_gemm_i8");
   int rc;
   if ((rc = gemm_checks(a, b, sa, sb, bias, out, acc_dbg, M, N, K, epilogue)) != SLIM_OK) return rc;
   if (M == 0) return SLIM_OK;
@@ -221,6 +226,7 @@ int slim_gemm_i8(const int8_t* a, const int8_t* b, const float* sa, const float*
 int slim_int8_linear(const void* x, int x_dtype, const int8_t* qw, const float* sw, const void* bias, void* out,
                      int8_t* xq_ws, float* sx_ws, int64_t M, int64_t N, int64_t K, int group, int epilogue,
                      void* stream) {
+  SLIM_NVTX("slim_int8_linear");
   int rc;
   if ((rc = check_group(K, group)) != SLIM_OK) return rc;
   if ((rc = check_dtype(x_dtype)) != SLIM_OK) return rc;
@@ -245,6 +251,7 @@ int slim_ffn_i8(const void* x, int x_dtype, const int8_t* w_up, const float* s_u
                 const int8_t* w_down, const float* s_down, const void* b_down, void* out, int8_t* xq_ws,
                 float* sx_ws, void* h_ws, int8_t* hq_ws, float* sh_ws, int64_t M, int64_t K, int64_t F, int act,
                 void* stream) {
+  SLIM_NVTX("slim_ffn_i8");
   if (act != kEpiGeluTanh && act != kEpiSwiGLU)
     return fail(SLIM_ERR_DTYPE, "FFN activation must be GELU-tanh (%d) or SwiGLU (%d), got %d", kEpiGeluTanh,
                 kEpiSwiGLU, act);
@@ -305,6 +312,7 @@ int slim_peer_close(void* ptr, int64_t offset) {
 
 int slim_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
                  void* stream) {
+  SLIM_NVTX("slim_copy_2d");
   if (height == 0 || width == 0) return SLIM_OK;
   if (dst == nullptr || src == nullptr) return fail(SLIM_ERR_NULL, "dst/src is NULL");
   if (width < 0 || height < 0 || dpitch < width || spitch < width) return fail(SLIM_ERR_SHAPE, "bad 2-D copy geometry");
@@ -318,6 +326,7 @@ int slim_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int
 int slim_int8_linear_colsplit(const void* x, int x_dtype, const int8_t* qw, const float* sw, const void* bias,
                               void* const* outs, int n_outs, int64_t ldo, int8_t* xq_ws, float* sx_ws, int64_t M,
                               int64_t N, int64_t K, int group, int epilogue, void* stream) {
+  SLIM_NVTX("slim_int8_linear_colsplit");
   int rc;
   if (outs == nullptr || n_outs < 1 || n_outs > kMaxPeers + 1)
     return fail(SLIM_ERR_SHAPE, "n_outs must be 1..%d, got %d", kMaxPeers + 1, n_outs);

@@ -44,6 +44,7 @@ extern "C" {
 
 int slim_nvfp4_pack(const void* w, int dtype, int64_t rows, int64_t K, uint8_t* q, uint8_t* block_scale,
                     float* tensor_scale, void* stream) {
+  SLIM_NVTX("slim_nvfp4_pack");
   int rc;
   if ((rc = check_dtype(dtype)) != SLIM_OK) return rc;
   if ((rc = nvfp4_k_checks(K, false)) != SLIM_OK) return rc;
@@ -64,6 +65,7 @@ int slim_nvfp4_pack(const void* w, int dtype, int64_t rows, int64_t K, uint8_t* 
 
 int slim_quant_nvfp4_act(const void* x, int dtype, int64_t rows, int64_t K, int rotate, uint8_t* q,
                          uint8_t* block_scale, float* row_scale, void* stream) {
+  SLIM_NVTX("slim_quant_nvfp4_act");
   int rc;
   if ((rc = check_dtype(dtype)) != SLIM_OK) return rc;
   if ((rc = nvfp4_k_checks(K, rotate != 0)) != SLIM_OK) return rc;
@@ -82,6 +84,7 @@ int slim_quant_nvfp4_act(const void* x, int dtype, int64_t rows, int64_t K, int 
 
 int slim_nvfp4_dequant(const uint8_t* q, const uint8_t* block_scale, const float* scale, int per_row, int64_t rows,
                        int64_t K, float* out, const void* x, int x_dtype, double* err, void* stream) {
+  SLIM_NVTX("slim_nvfp4_dequant");
   int rc;
   if ((rc = nvfp4_k_checks(K, false)) != SLIM_OK) return rc;
   if (rows < 0) return fail(SLIM_ERR_SHAPE, "negative row count");
@@ -104,6 +107,7 @@ int slim_nvfp4_dequant(const uint8_t* q, const uint8_t* block_scale, const float
 int slim_gemm_nvfp4(const uint8_t* a, const uint8_t* a_sf, const float* a_scale, const uint8_t* b,
                     const uint8_t* b_sf, const float* b_scale, const void* bias, void* out, float* acc_dbg, int64_t M,
                     int64_t N, int64_t K, int epilogue, void* stream) {
+  SLIM_NVTX("slim_gemm_nvfp4");
   int rc;
   if ((rc = nvfp4_gemm_checks(a, a_sf, a_scale, b, b_sf, b_scale, bias, out, acc_dbg, M, N, K, epilogue)) != SLIM_OK)
     return rc;
@@ -119,6 +123,7 @@ int slim_gemm_nvfp4(const uint8_t* a, const uint8_t* a_sf, const float* a_scale,
 int slim_nvfp4_linear(const void* x, int x_dtype, const uint8_t* qw, const uint8_t* w_sf, const float* w_scale,
                       const void* bias, void* out, uint8_t* xq_ws, uint8_t* xsf_ws, float* xs_ws, int64_t M, int64_t N,
                       int64_t K, int rotate, int epilogue, void* stream) {
+  SLIM_NVTX("slim_nvfp4_linear");
   int rc;
   if ((rc = check_dtype(x_dtype)) != SLIM_OK) return rc;
   if ((rc = nvfp4_k_checks(K, rotate != 0)) != SLIM_OK) return rc;

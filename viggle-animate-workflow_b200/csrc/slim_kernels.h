@@ -3,11 +3,24 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
+
 #include <cstddef>
 #include <cstdint>
 #include <mutex>
 
 namespace slim {
+
+// NVTX range around a C-ABI entry point, so that a profiler's timeline groups each call's
+// kernel launches under the entry's name (header-only NVTX v3: without a profiler attached
+// the push/pop calls return at once).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
+#define SLIM_NVTX(name) ::slim::NvtxRange slim_nvtx_range_(name)
 
 // Lazy per-device initialisation for the launchers' caches (kernel attributes, occupancy):
 // run() calls init once per device under a lock, later calls only check the flag; an init that

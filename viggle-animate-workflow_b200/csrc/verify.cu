@@ -122,6 +122,7 @@ extern "C" {
 
 int slim_rel_l2_int8(const int8_t* qa, const float* sa, const int8_t* qb, const float* sb, int64_t rows, int64_t K,
                      double* out2, void* stream) {
+  SLIM_NVTX("slim_rel_l2_int8");
   int rc;
   if (rows < 0 || K <= 0 || K % 16 != 0) return fail(SLIM_ERR_SHAPE, "rel_l2_int8 needs K %% 16 == 0, got %lld", static_cast<long long>(K));
   if (rows == 0) return SLIM_OK;
@@ -137,6 +138,7 @@ int slim_rel_l2_int8(const int8_t* qa, const float* sa, const int8_t* qb, const 
 }
 
 int slim_rel_l2(const void* a, int a_dtype, const void* b, int b_dtype, int64_t n, double* out2, void* stream) {
+  SLIM_NVTX("slim_rel_l2");
   int rc;
   if ((rc = check_dtype(a_dtype)) != SLIM_OK) return rc;
   if ((rc = check_dtype(b_dtype)) != SLIM_OK) return rc;
