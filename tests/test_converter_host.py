@@ -204,6 +204,59 @@ def test_multi_process_split_writes_the_same_bytes(official_dir, golden_meta, tm
     assert hashlib.sha256(out.read_bytes()).hexdigest() == golden_meta["convert_block0"]["sha256_file"]
 
 
+def _failing_worker(rank, world, port, src, out, result_dir, mode):
+    """Rank 1 fails: "raise" makes its writes raise inside its share of the work; "absent" makes
+    it leave right after joining the process group, never entering the conversion."""
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, init_method=f"tcp://127.0.0.1:{port}",
+                            timeout=datetime.timedelta(seconds=10))
+    outcome = "ok"
+    try:
+        if rank == 1 and mode == "absent":
+            outcome = "absent"
+            return
+        if rank == 1 and mode == "raise":
+            def broken_write(self, name, payload):
+                raise RuntimeError("injected write failure")
+            OffsetWriter.write = broken_write
+        convert(src, out, rank=8, grid=65, block_limit=0)
+    except BaseException as exc:  # noqa: BLE001 - the outcome is what the test checks
+        outcome = f"{type(exc).__name__}: {exc}"
+    finally:
+        Path(result_dir, f"rank{rank}.txt").write_text(outcome)
+        if not (rank == 1 and mode == "absent"):
+            try:
+                dist.destroy_process_group()
+            except Exception:  # noqa: BLE001
+                pass
+
+
+@pytest.mark.parametrize("mode", ["raise", "absent"])
+def test_a_failing_rank_fails_every_rank_and_removes_the_partial_output(official_dir, tmp_path, mode):
+    """Failure detection across ranks: every rank that reaches a synchronisation point learns of
+    the failure (rank 0 from the all-reduce of the ranks' success flags, or from the collective
+    erroring when a rank is gone), raises, and the pre-sized output file is removed."""
+    import time
+
+    import torch.multiprocessing as mp
+    out = tmp_path / "split.safetensors"
+    t0 = time.time()
+    mp.start_processes(_failing_worker, args=(2, _free_port(), str(official_dir), str(out), str(tmp_path), mode),
+                       nprocs=2, join=True, start_method="spawn")
+    assert time.time() - t0 < 120
+    r0 = (tmp_path / "rank0.txt").read_text()
+    r1 = (tmp_path / "rank1.txt").read_text()
+    assert r0 != "ok" and "RuntimeError" in r0, r0
+    if mode == "raise":
+        assert "another rank" in r0 and "injected write failure" in r1, (r0, r1)
+    else:
+        assert r1 == "absent"
+    assert not out.exists()
+
+
 def test_byte_level_copies_equal_the_torch_path(tmp_path):
     """Copy/concat ops assembled from the stored bytes (positional reads, half swaps, exact
     bf16 -> f32 widening) give the bytes of the torch cast path the reference uses."""

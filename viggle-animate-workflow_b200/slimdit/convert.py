@@ -132,11 +132,6 @@ def _dist():
     return 0, 1
 
 
-def _barrier(workers: int) -> None:
-    if workers > 1:
-        torch.distributed.barrier()
-
-
 class _GpuQuantizer:
     """Quantises one linear on this process's GPU: H2D of the bf16 sources (concatenated and
     half-swapped while copying), reference-order rotate + INT8, D2H of codes and scales; the
@@ -371,9 +366,56 @@ def convert(src_dir: str | Path, out_path: str | Path, rank: int = 8, grid: int 
     reads, GPU work and writes across the INT8 linears (``_Pipeline``) and runs the curve
     basis and the curve, copy and derived tensors on four host threads alongside (copies as
     positional byte moves, the adaLN weights widened from their stored bf16 bytes);
-    ``pipeline=False`` takes the ops one at a time. Both write the same bytes.
+    ``pipeline=False`` takes the ops one at a time. Both write the same bytes. If the
+    conversion fails on any rank, every rank raises and the partial output file is removed
+    (the positional writer sizes the file up front, so a partial one would look complete).
     """
+
     worker, workers = _dist()
+    steps = _convert_steps(src_dir, out_path, rank, grid, block_limit, verify_blocks, curve_dtype, metadata, quant,
+                           quant_report, pipeline, worker, workers)
+    # Two synchronisation points: after rank 0 has created the output file, and after every
+    # rank has written its tensors. At each, every rank reports whether its part succeeded (a
+    # MIN all-reduce, reached by failing ranks too); on any failure rank 0 removes the partial
+    # output (pre-sized, it would look complete) and every rank raises.
+    for _ in range(2):
+        failure = None
+        try:
+            next(steps)
+        except BaseException as exc:  # noqa: BLE001 - re-raised below, after the collective
+            failure = exc
+        if not _all_ok(failure is None, workers):
+            steps.close()
+            if worker == 0:
+                Path(out_path).unlink(missing_ok=True)
+            if failure is not None:
+                raise failure
+            raise RuntimeError("conversion failed on another rank; the partial output was removed")
+    try:
+        next(steps)
+    except StopIteration as done:
+        return done.value
+    raise AssertionError("conversion steps did not finish")  # pragma: no cover
+
+
+def _all_ok(ok: bool, workers: int) -> bool:
+    """True when this rank and (under torch.distributed) every other rank succeeded. A peer
+    that died or never joined makes the collective raise (process-group timeout): not ok."""
+    if workers == 1:
+        return ok
+    try:
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32)
+        if torch.distributed.get_backend() == "nccl":
+            flag = flag.cuda()
+        torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MIN)
+        return bool(flag.item())
+    except Exception:  # noqa: BLE001 - a failed collective means some rank did not succeed
+        return False
+
+
+def _convert_steps(src_dir, out_path, rank, grid, block_limit, verify_blocks, curve_dtype, metadata, quant,
+                   quant_report, pipeline, worker, workers):
+    """The body of ``convert``; yields at its two synchronisation points (see there)."""
     src = ShardSet(src_dir)
     ops = mapping.build_plan(src.manifest.keys())
     missing = mapping.missing_sources(ops, src.manifest)
@@ -388,7 +430,13 @@ def convert(src_dir: str | Path, out_path: str | Path, rank: int = 8, grid: int 
     t0 = time.time()
     if worker == 0:
         writer = OffsetWriter(out_path, manifest, metadata or {"format": "pt"}, create=True)
-    _barrier(workers)
+    try:
+        yield  # synchronisation point 1: the output file exists
+    except GeneratorExit:  # another rank failed: release the files and stop
+        if worker == 0:
+            writer.close()
+        src.close()
+        raise
     if worker != 0:
         writer = OffsetWriter(out_path, manifest, metadata or {"format": "pt"}, create=False)
 
@@ -492,7 +540,7 @@ def convert(src_dir: str | Path, out_path: str | Path, rank: int = 8, grid: int 
     expect = {n for op in mine for n in _outputs(op, quant)} | ({"adaln_t_table"} if worker == 0 else set())
     writer.close(expect=expect)
     src.close()
-    _barrier(workers)
+    yield  # synchronisation point 2: every rank's tensors are written
     if workers > 1:
         gathered: list = [None] * workers
         torch.distributed.all_gather_object(gathered, report.quant_errors)
