@@ -12,7 +12,7 @@ carries into the exponent (-126.54 -> -64), so the rotated quantiser, ``quant_fp
 and ``flash_int8`` cannot be executed faithfully here. The unrotated quantiser and the amax
 use only fp32 loads, max, division, floor and clamps, which the interpreter runs with numpy.
 
-    python tests/golden/make_attention_golden.py [path to attention_triton.py]
+    python tests/golden/make_attention_golden.py <reference tree>/comfyui/ComfyUI-SlimDiT/attention_triton.py
 """
 
 from __future__ import annotations
@@ -29,7 +29,6 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
-DEFAULT_REF = "/root/reference/comfyui/ComfyUI-SlimDiT/attention_triton.py"
 CASES = [(100, 2, 11), (37, 3, 12), (200, 1, 13)]  # (tokens, heads, seed)
 D = 128
 
@@ -79,4 +78,6 @@ def main(ref_path: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else DEFAULT_REF)
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_attention_golden.py <path to the reference's attention_triton.py>")
+    main(sys.argv[1])

@@ -1,8 +1,8 @@
 """Generate the golden fixtures by running the REFERENCE's own slimdit code.
 
-Run in a container where the reference tree is mounted (read-only) at /root/reference:
+Run in a container where the reference tree is mounted (read-only), giving its path:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <path to the reference tree>
 
 It imports the reference's ``slimdit`` package by path and records, on seeded synthetic
 inputs (tests/synthetic.py):
@@ -11,6 +11,9 @@ inputs (tests/synthetic.py):
   * dequantize_convrot_weight outputs;
   * per-token activation quantisation with the reference's own math (rotate + int8.py:49-51);
   * SHA-256 of the full weight conversion of W [5120, 5120];
+  * SHA-256 of the reference's per-token codes and scales (rotate() + int8.py:49-51 per row) of
+    8192 x 5120 activations and a 2048 x 13824 FFN hidden, with the number of codes and scales
+    the butterfly order changes on them;
   * the descriptor blob, and the bytes (SHA-256 + header) of reference convert() runs on a
     2-block synthetic official checkpoint (full, and with block_limit=0);
   * the NVFP4 host contract of slimdit/nvfp4.py that needs no comfy_kitchen: descriptor
@@ -45,6 +48,10 @@ WEIGHT_CASES = [  # name, rows, K, seed
     ("w_k13824", 8, 13824, 107),
 ]
 ACT_CASES = [("x_k5120", 16, 5120, 201), ("x_k13824", 8, 13824, 202)]
+SCALE_CASES = [  # name, synthetic generator, rows, K, seed
+    ("act_8192x5120", "activations", 8192, 5120, 1),
+    ("hidden_2048x13824", "ffn_hidden", 2048, 13824, 3),
+]
 CONVERT_CASE = {"n_blocks": 2, "hidden": 512, "ffn": 1024, "time_hidden": 64, "seed": 7, "n_shards": 2}
 
 
@@ -79,7 +86,7 @@ def nvfp4_contract(src_dir) -> dict:
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of the reference tree (its slimdit package is imported)")
     ap.add_argument("--skip-config0", action="store_true")
     args = ap.parse_args(argv)
     sys.path.insert(0, args.reference)
@@ -123,6 +130,24 @@ def main(argv=None) -> int:
             "sha256_q": sha256(q0.tobytes()),
             "sha256_scale": sha256(s0.tobytes()),
             "q_min": int(q0.min()), "q_max": int(q0.max()),
+        }
+
+    # at-scale activation rows: the reference's own per-row math on token rows
+    sys.path.insert(0, str(HERE.parent.parent))
+    import oracle  # noqa: E402  (butterfly order, for the recorded mismatch counts only)
+
+    meta["at_scale"] = {}
+    for name, gen, rows, k, seed in SCALE_CASES:
+        x = getattr(synthetic, gen)(rows, k, seed=seed)
+        q, s = quantize_convrot_weight(x)
+        qb, sb = oracle.quantize_activations(x)
+        meta["at_scale"][name] = {
+            "generator": gen, "rows": rows, "K": k, "seed": seed,
+            "sha256_input_bf16": sha256(synthetic.f32_to_bf16_bits(x).tobytes()),
+            "sha256_q": sha256(q.tobytes()), "sha256_scale": sha256(s.tobytes()),
+            "butterfly_codes_differ": int((q != qb).sum()),
+            "butterfly_code_max_abs_diff": int(np.abs(q.astype(np.int32) - qb.astype(np.int32)).max()),
+            "butterfly_scales_differ": int((s.view(np.uint32) != sb.view(np.uint32)).sum()),
         }
 
     with tempfile.TemporaryDirectory() as tmp:

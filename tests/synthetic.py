@@ -51,6 +51,17 @@ def activations(rows: int, cols: int, seed: int = 1, nu: float = 4.0, scale: flo
     return bf16_round_f32(x)
 
 
+def ffn_hidden(rows: int, cols: int, seed: int = 3) -> np.ndarray:
+    """A GELU-shaped FFN hidden [rows, cols] in bf16: h = u * s(1.702 u), s(z) = (1 + z / (1 + |z|)) / 2,
+    u = 2 * activations(rows, cols, seed). Rational arithmetic only (every operation correctly rounded),
+    so the values are the same on any host; like GELU it keeps large positive inputs and squeezes
+    negative ones towards zero, which gives each 256-group a wide spread of magnitudes."""
+    u = activations(rows, cols, seed=seed) * np.float32(2.0)
+    z = u * np.float32(1.702)
+    s = (np.float32(1.0) + z / (np.float32(1.0) + np.abs(z))) * np.float32(0.5)
+    return bf16_round_f32((u * s).astype(np.float32))
+
+
 # --------------------------------------------------------------------------- checkpoints
 # Official key layout of one MiniMax-H3 transformer (the key template of the reference's
 # tests/test_mapping.py:6-59), with shapes scaled by `hidden` / `ffn` / `time_hidden`.

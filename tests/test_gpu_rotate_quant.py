@@ -237,3 +237,73 @@ def test_dequantize_from_unaligned_codes_matches_aligned(cuda):
     shifted.copy_(q)
     assert shifted.data_ptr() % 16 != 0
     assert torch.equal(ops.dequantize(shifted, scale).view(torch.int32), ops.dequantize(q, scale).view(torch.int32))
+
+
+@pytest.mark.parametrize("name", ["act_8192x5120", "hidden_2048x13824"])
+def test_reference_order_activations_at_scale_vs_reference_digests(cuda, golden_meta, name):
+    """Per-token codes and scales in the reference order at scale: SHA-256 equal to the
+    reference's own outputs; the butterfly order's differences from them are counted exactly."""
+    from slimdit import ops
+    meta = golden_meta["at_scale"][name]
+    x = getattr(synthetic, meta["generator"])(meta["rows"], meta["K"], seed=meta["seed"])
+    b16 = synthetic.f32_to_bf16_bits(x)
+    assert hashlib.sha256(b16.tobytes()).hexdigest() == meta["sha256_input_bf16"]
+    xt = bf16_tensor(b16, cuda)
+    q, s = ops.rotate_quant(xt, order="reference")
+    qn, sn = q.cpu().numpy(), s.cpu().numpy()
+    assert hashlib.sha256(qn.tobytes()).hexdigest() == meta["sha256_q"]
+    assert hashlib.sha256(sn.tobytes()).hexdigest() == meta["sha256_scale"]
+    qb, sb = ops.rotate_quant(xt, order="butterfly")
+    qb, sb = qb.cpu().numpy(), sb.cpu().numpy()
+    assert int((qn != qb).sum()) == meta["butterfly_codes_differ"]
+    assert int(np.abs(qn.astype(np.int32) - qb.astype(np.int32)).max()) == meta["butterfly_code_max_abs_diff"]
+    assert int((bits(sn) != bits(sb)).sum()) == meta["butterfly_scales_differ"]
+
+
+def _stress_rows(k: int, dtype) -> np.ndarray:
+    """Rows that drive every branch of the certified quantiser: wide dynamic ranges (many
+    inexact groups and queued outputs), integer rows (exact ties), a spike over tiny noise (many
+    outputs tied for the row maximum), zero, constant, tiny and heavy-tailed rows."""
+    rng = np.random.default_rng(k)
+    hi = 12 if dtype == torch.float16 else 40
+    lo = -12 if dtype == torch.float16 else -40
+    rows = []
+    for _ in range(24):  # log-uniform magnitudes with random signs
+        mag = np.exp2(rng.uniform(lo, hi, size=k))
+        rows.append(mag * rng.choice([-1.0, 1.0], size=k))
+    for _ in range(8):
+        rows.append(rng.integers(-3, 4, size=k).astype(np.float64))
+    for _ in range(4):
+        r = rng.standard_normal(k) * 1e-3
+        r[rng.integers(0, k)] = 50.0
+        rows.append(r)
+    rows.append(np.zeros(k))
+    rows.append(np.full(k, 0.75))
+    rows.append(rng.standard_normal(k) * (1e-4 if dtype == torch.float16 else 1e-30))
+    rows.extend(synthetic.activations(16, k, seed=k + 5).astype(np.float64))
+    rows.extend(synthetic.ffn_hidden(16, k, seed=k + 6).astype(np.float64))
+    return np.stack(rows).astype(np.float32)
+
+
+@pytest.mark.parametrize("k", [1280, 2816, 5120, 13824, 16384])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_certified_reference_order_stress_vs_oracle(cuda, k, dtype):
+    from slimdit import ops
+    xt = torch.from_numpy(_stress_rows(k, dtype)).to(cuda).to(dtype)
+    xin = xt.float().cpu().numpy()
+    q, s = ops.rotate_quant(xt, order="reference")
+    qo, so = oracle.quantize_rows(oracle.rotate_reference(xin))
+    assert np.array_equal(bits(s.cpu().numpy()), bits(so))
+    assert np.array_equal(q.cpu().numpy(), qo)
+
+
+@pytest.mark.parametrize("rows", [1, 3, 997, 4096])
+def test_certified_reference_order_many_rows_vs_oracle(cuda, rows):
+    """Row counts below, near and far above the persistent grid (queues carried across rows)."""
+    from slimdit import ops
+    x = synthetic.ffn_hidden(rows, 5120, seed=rows)
+    xt = torch.from_numpy(x).to(cuda).to(torch.bfloat16)
+    q, s = ops.rotate_quant(xt, order="reference")
+    qo, so = oracle.quantize_convrot_weight(x)
+    assert np.array_equal(bits(s.cpu().numpy()), bits(so))
+    assert np.array_equal(q.cpu().numpy(), qo)

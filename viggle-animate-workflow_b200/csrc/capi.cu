@@ -146,6 +146,8 @@ int slim_rotate_quant_i8(const void* x, int dtype, int64_t rows, int64_t K, int 
       if (e != cudaSuccess) return cuda_fail(e, "rotate launch");
       note_launch();
       e = launch_quantize_rows(rot_out, rows, static_cast<int>(K), q, scale, st);
+    } else if (cert_supported(rows, K)) {
+      e = launch_cert_rotate_quant(x, dtype, rows, static_cast<int>(K), q, scale, st);
     } else {
       e = launch_ref_rotate_quant(x, dtype, rows, static_cast<int>(K), q, scale, st);
     }

@@ -3,6 +3,7 @@
 #include "capi.cu"
 #include "gemm_i8.cu"
 #include "rotate_quant.cu"
+#include "cert_quant.cu"
 #include "linear_noalloc.cu"
 #include "nvfp4_quant.cu"
 #include "gemm_nvf4.cu"
