@@ -180,7 +180,8 @@ def make_inputs(torch, dev, seed: int = 0):
 # ----------------------------------------------------------------------------- CPU baseline
 def cpu_linear_sample(rows: int, seed: int = 0):
     """CPU restatement of the convrot linear on `rows` tokens of the QKV linear (K 5120, N 15360):
-    oracle rotation (C, butterfly order) + the reference's quantisation math (numpy) +
+    the reference's rotation (np.matmul of the grouped rows with H^T, slimdit/hadamard.py:56-58,
+    numpy/OpenBLAS on all host threads) + its per-row quantisation math (slimdit/int8.py:49-51) +
     torch's CPU int8 GEMM + fp32 dequant. Returns (seconds, threads)."""
     import numpy as np
     import torch
@@ -193,7 +194,9 @@ def cpu_linear_sample(rows: int, seed: int = 0):
     qw = torch.from_numpy(rng.integers(-127, 128, size=(N, K), dtype=np.int8))
     sw = torch.from_numpy((rng.random(N, dtype=np.float32) * 1e-3).astype(np.float32))
     t0 = time.perf_counter()
-    qx, sx = oracle.quantize_activations(x)
+    h = oracle.build_hadamard(256)
+    rot = np.matmul(x.reshape(rows, K // 256, 256), h.T).reshape(rows, K)
+    qx, sx = oracle.quantize_rows(rot)
     acc = torch._int_mm(torch.from_numpy(qx), qw.t())
     y = (acc.float() * torch.from_numpy(sx) * sw[None, :]).to(torch.bfloat16)
     dt = time.perf_counter() - t0

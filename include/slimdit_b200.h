@@ -15,9 +15,14 @@
  *   SLIM_ORDER_REFERENCE reproduces the reference's fp32 summation order of
  *     `np.matmul(grouped, H.T)` (slimdit/hadamard.py:56-58, numpy 2.3 + OpenBLAS 0.3.30
  *     on x86-64), so codes and scales equal slimdit.int8.quantize_convrot_weight's bit for
- *     bit. Compute-bound (~256 fp32 FMAs per element).
- *   SLIM_ORDER_BUTTERFLY is the radix-4 fast Hadamard transform (memory-bound), used for
- *     activations.
+ *     bit. For rows of 5..64 groups (K = 1280..16384) with rot_out NULL it runs at the cost
+ *     of the fast transform (a certified butterfly: the reference's sequential chains are
+ *     evaluated only for the few outputs whose code or whose row maximum they can change);
+ *     otherwise compute-bound (~256 fp32 FMAs per element). The linears below quantise their
+ *     activations in this order.
+ *   SLIM_ORDER_BUTTERFLY is the radix-4 fast Hadamard transform alone (memory-bound): a few
+ *     codes per million and ~4 % of row scales differ from the reference's (counted by the
+ *     tests and the benchmark).
  */
 #ifndef SLIMDIT_B200_H_
 #define SLIMDIT_B200_H_
@@ -73,9 +78,9 @@ int slim_rotate_f32(const void* x, int dtype, int64_t rows, int64_t K, int group
 
 /* Rotation fused with per-row symmetric INT8 quantisation:
  *   scale[r] = max(absmax_r / 127, 1e-30),  q = clip(rint(rot / scale), -128, 127).
- * Replaces slimdit.int8.quantize_convrot_weight (slimdit/int8.py:39-52) for weights
- * (order REFERENCE) and the per-token activation quantisation inside the runtime's
- * int8_linear (tools/bench_int8.py:65-68) (order BUTTERFLY).
+ * Replaces slimdit.int8.quantize_convrot_weight (slimdit/int8.py:39-52) for weights and the
+ * per-token activation quantisation inside the runtime's int8_linear
+ * (tools/bench_int8.py:65-68), the same per-row math applied to token rows.
  * q: int8 [rows, K]; scale: fp32 [rows]; rot_out: optional fp32 [rows, K] copy of the
  * rotated values (NULL to skip). BUTTERFLY requires K <= 16384. */
 int slim_rotate_quant_i8(const void* x, int dtype, int64_t rows, int64_t K, int group,
@@ -102,7 +107,7 @@ int slim_gemm_i8(const int8_t* a, const int8_t* b, const float* sa, const float*
                  int64_t K, int epilogue, void* stream);
 
 /* The convrot W8A8 linear: rotate + quantise the bf16/f16/f32 activation x [M,K] per
- * token (BUTTERFLY order) into the caller's workspaces xq_ws (int8 [M,K]) and sx_ws
+ * token (REFERENCE order) into the caller's workspaces xq_ws (int8 [M,K]) and sx_ws
  * (fp32 [M]), then slim_gemm_i8 against the pre-rotated weight codes qw [N,K] with row
  * scales sw [N]. Drop-in for comfy_kitchen.int8_linear(x, qweight, wscales, convrot=True,
  * convrot_groupsize=256, out_dtype=bf16) (tools/bench_int8.py:65-68). */
@@ -132,10 +137,10 @@ int slim_ffn_i8(const void* x, int x_dtype, const int8_t* w_up, const float* s_u
  * Same arguments and result as slim_int8_linear, minus xq_ws/sx_ws: the activation codes
  * and scales go to one 32 MiB array compiled into the library, which every GPU that loads
  * the library holds until exit. Limit: round_up(M*K, 256) + 4*M <= 32 MiB (e.g. 6400
- * tokens at K = 5120); larger calls return SLIM_ERR_SHAPE. The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress); make it before any stream
- * capture. All calls share the array: calls that overlap on the GPU race. Allocates
- * nothing (no cudaMalloc/cudaFree). */
+ * tokens at K = 5120); larger calls return SLIM_ERR_SHAPE. The first call on a device (and
+ * again the first in another CUDA context of it) looks up the array's device address
+ * (cudaGetSymbolAddress); make it before any stream capture. All calls share the array:
+ * calls that overlap on the GPU race. Allocates nothing (no cudaMalloc/cudaFree). */
 int slim_int8_linear_noalloc(const void* x, int x_dtype, const int8_t* qw, const float* sw,
                              const void* bias, void* out, int64_t M, int64_t N, int64_t K,
                              int group, int epilogue, void* stream);
@@ -176,8 +181,9 @@ int slim_int8_linear_colsplit(const void* x, int x_dtype, const int8_t* qw, cons
                               int group, int epilogue, void* stream);
 
 /* ---------------------------------------------------------------- NVFP4
- * Format of slimdit/nvfp4.py:3-8: E2M1 codes packed two per byte (element 2i in the low
- * nibble), one UE4M3 scale per 16 consecutive elements along K stored in the cuBLAS 128x4
+ * Format of slimdit/nvfp4.py:3-8: E2M1 codes packed two per byte, high nibble first (element
+ * 2i in the high nibble, 2i+1 in the low one; activations too, so that both operands of the
+ * FP4 GEMM share the order), one UE4M3 scale per 16 consecutive elements along K stored in the cuBLAS 128x4
  * tiled layout (scale (r, c) of a [R, C = K/16] matrix at byte
  * ((r/128)*(C/4) + c/4)*512 + (r%32)*16 + ((r%128)/32)*4 + c%4), and an fp32 global scale
  * gs = amax / (448 * 6). Block scale = e4m3(min(fl(fl(block_amax / 6) / gs), 448)); codes =

@@ -27,11 +27,9 @@ Cross-check (tests/test_gpu_nvfp4.py): flashinfer's fp4_quantize, NVIDIA's NVFP4
 gives the same block-scale bytes in the same tiled layout and the same codes except where its
 reciprocal-multiply rounding and this recipe's division straddle a grid midpoint (one step).
 
-Nibble order: element 2i of a row goes to the LOW nibble of byte i, element 2i+1 to the
-high nibble. This is the order the tensor cores (and cuBLAS' packed E2M1 operands) read.
-The reference docstring says "high nibble first" (slimdit/nvfp4.py:5); that wording cannot
-be checked against comfy_kitchen here, and the layout the runtime's FP4 GEMM consumes is
-the hardware order, so this restatement follows the hardware.
+Nibble order: "two E2M1 values per byte, high nibble first" (slimdit/nvfp4.py:5,
+docs/DEV_NOTES.md:64): element 2i of a row goes to the HIGH nibble of byte i, element 2i+1 to
+the low nibble.
 
 An all-zero tensor (s2 = 0) quantises to zero codes and zero scales here; the recipe as
 written would divide 0 by 0.
@@ -103,16 +101,16 @@ def e2m1_decode(c: np.ndarray) -> np.ndarray:
 
 
 def pack_nibbles(codes: np.ndarray) -> np.ndarray:
-    """[R, K] 4-bit codes -> [R, K/2] bytes, element 2i in the low nibble."""
+    """[R, K] 4-bit codes -> [R, K/2] bytes, high nibble first (element 2i in the high nibble)."""
     codes = np.asarray(codes, dtype=np.uint8)
-    return (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)
+    return ((codes[:, 0::2] << 4) | codes[:, 1::2]).astype(np.uint8)
 
 
 def unpack_nibbles(packed: np.ndarray) -> np.ndarray:
     packed = np.asarray(packed, dtype=np.uint8)
     out = np.empty((packed.shape[0], packed.shape[1] * 2), dtype=np.uint8)
-    out[:, 0::2] = packed & 0xF
-    out[:, 1::2] = packed >> 4
+    out[:, 0::2] = packed >> 4
+    out[:, 1::2] = packed & 0xF
     return out
 
 

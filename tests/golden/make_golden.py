@@ -140,7 +140,7 @@ def main(argv=None) -> int:
     for name, gen, rows, k, seed in SCALE_CASES:
         x = getattr(synthetic, gen)(rows, k, seed=seed)
         q, s = quantize_convrot_weight(x)
-        qb, sb = oracle.quantize_activations(x)
+        qb, sb = oracle.quantize_activations(x, order="butterfly")
         meta["at_scale"][name] = {
             "generator": gen, "rows": rows, "K": k, "seed": seed,
             "sha256_input_bf16": sha256(synthetic.f32_to_bf16_bits(x).tobytes()),

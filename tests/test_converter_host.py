@@ -281,3 +281,20 @@ def test_byte_level_copies_equal_the_torch_path(tmp_path):
         checked += 1
     src.close()
     assert checked >= 20
+
+
+@pytest.mark.parametrize("pipeline", [True, False])
+def test_a_failing_host_job_closes_the_files_and_removes_the_output(official_dir, tmp_path, monkeypatch, pipeline):
+    """A host-side op that raises during the write phase (here the curve projection): the
+    conversion raises that error, the host threads are stopped, no file descriptor is left open
+    and the pre-sized partial output is removed."""
+    def fail(*args, **kwargs):
+        raise RuntimeError("injected projection failure")
+
+    monkeypatch.setattr(curve_mod, "project_weight", fail)
+    out = tmp_path / "failed.safetensors"
+    fds_before = len(os.listdir("/proc/self/fd"))
+    with pytest.raises(RuntimeError, match="injected projection failure"):
+        convert(official_dir, out, rank=8, grid=65, block_limit=0, pipeline=pipeline)
+    assert not out.exists()
+    assert len(os.listdir("/proc/self/fd")) <= fds_before

@@ -108,9 +108,9 @@ def test_gemm_shape_errors(cuda):
 
 @pytest.mark.parametrize("m,n,k", [(256, 768, 5120), (77, 512, 1024), (4096, 1536, 5120)])
 def test_int8_linear_end_to_end_vs_oracle(cuda, m, n, k):
-    """x bf16 -> butterfly rotate + per-token INT8 -> GEMM -> bf16; weights from the reference
-    converter path. Codes bit-exact with the oracle's; output within 1 bf16 ulp of the fp64
-    dequant of those codes."""
+    """x bf16 -> rotate + per-token INT8 (the reference's order) -> GEMM -> bf16; weights from
+    the reference converter path. Codes bit-exact with the oracle's; output within 1 bf16 ulp of
+    the fp64 dequant of those codes."""
     from slimdit import ops
     from slimdit.int8 import quantize_convrot_weight
     x = synthetic.activations(m, k, seed=m + n)

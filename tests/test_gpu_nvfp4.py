@@ -281,8 +281,9 @@ def test_cross_check_against_flashinfer_nvfp4(cuda):
         fq = fq.view(torch.uint8).reshape(m, k // 2).cpu().numpy()
         fsf = fsf.view(torch.uint8).reshape(-1)[: m * k // 16].reshape(m, k // 16).cpu().numpy()
         assert np.array_equal(sf.cpu().numpy().reshape(m, k // 16), fsf), "block scale bytes differ"
-        ours = q.cpu().numpy()
-        a = np.stack([ours & 15, ours >> 4], -1).reshape(m, k).astype(np.int16)
+        # flashinfer packs element 2i in the low nibble (the hardware's own operand order); the
+        # stored layout here is high nibble first, so the codes are compared element by element
+        a = onv.unpack_nibbles(q.cpu().numpy()).astype(np.int16)
         b = np.stack([fq & 15, fq >> 4], -1).reshape(m, k).astype(np.int16)
         diff = a != b
         assert diff.mean() < 1e-3, diff.mean()

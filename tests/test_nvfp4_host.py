@@ -110,11 +110,28 @@ def test_blocked_layout_index_formula_and_round_trip():
     assert np.array_equal(onv.from_blocked(onv.to_blocked(sf), r, c), sf)
 
 
-def test_pack_nibbles_low_nibble_first():
+def test_pack_nibbles_high_nibble_first():
+    """"two E2M1 values per byte, high nibble first" (slimdit/nvfp4.py:5, docs/DEV_NOTES.md:64)."""
     codes = np.array([[1, 2, 3, 4, 15, 8]], dtype=np.uint8)
     packed = onv.pack_nibbles(codes)
-    assert packed.tolist() == [[0x21, 0x43, 0x8F]]
+    assert packed.tolist() == [[0x12, 0x34, 0xF8]]
     assert np.array_equal(onv.unpack_nibbles(packed), codes)
+
+
+def test_on_disk_bytes_of_a_known_block():
+    """A 2 x 16 weight whose every element sits on the E2M1 grid: the packed bytes put element
+    2i in the high nibble (E2M1 codes: 0.5 -> 1, 1 -> 2, 1.5 -> 3, 2 -> 4, 3 -> 5, 4 -> 6,
+    6 -> 7, sign bit 8). With the global scale amax / 2688 a block whose maximum is 6 gets the
+    block scale 448 (UE4M3 0x7E), so global x block scale = 1 and the values are their codes."""
+    row = np.array([6, -6, 0.5, 1, 1.5, 2, 3, 4, -0.5, -1, -1.5, -2, -3, -4, 0, 6], np.float32)
+    w = np.zeros((128, 64), np.float32)
+    w[0, :16] = row
+    w[1, :16] = row[::-1]
+    q, sf, gs = onv.quantize_nvfp4_weight(w)
+    assert gs == np.float32(np.float32(6.0) / np.float32(2688.0))
+    assert q[0, :8].tolist() == [0x7F, 0x12, 0x34, 0x56, 0x9A, 0xBC, 0xDE, 0x07]
+    assert q[1, :8].tolist() == [0x70, 0xED, 0xCB, 0xA9, 0x65, 0x43, 0x21, 0xF7]
+    assert onv.from_blocked(sf, 128, 4)[0, 0] == 0x7E and onv.from_blocked(sf, 128, 4)[1, 0] == 0x7E
 
 
 def test_oracle_weight_recipe_round_trip_error_is_nvfp4_sized():

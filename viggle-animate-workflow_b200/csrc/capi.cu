@@ -65,6 +65,15 @@ static int check_dtype(int dtype) {
   return SLIM_OK;
 }
 
+// The activation side of the linears: per-token rotation + INT8 in the reference's order
+// (slimdit/hadamard.py:56-58 with slimdit/int8.py:49-51 per row), so the activation codes and
+// scales are the reference's bit for bit: the certified kernel for rows of 5..64 groups, the
+// reference-order kernels otherwise.
+cudaError_t launch_act_quant(const void* x, int dtype, int64_t rows, int K, int8_t* q, float* scale, cudaStream_t st) {
+  if (cert_supported(rows, K)) return launch_cert_rotate_quant(x, dtype, rows, K, q, scale, st);
+  return launch_ref_rotate_quant(x, dtype, rows, K, q, scale, st);
+}
+
 }  // namespace slim
 
 using namespace slim;
@@ -239,7 +248,7 @@ int slim_int8_linear(const void* x, int x_dtype, const int8_t* qw, const float* 
   if (!aligned16(x)) return fail(SLIM_ERR_ALIGN, "x must be 16-byte aligned");
   if ((rc = check_arch()) != SLIM_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = launch_bfly_rotate_quant(x, x_dtype, M, static_cast<int>(K), xq_ws, sx_ws, nullptr, st);
+  cudaError_t e = launch_act_quant(x, x_dtype, M, static_cast<int>(K), xq_ws, sx_ws, st);
   if (e != cudaSuccess) return cuda_fail(e, "activation quant launch");
   note_launch();
   GemmI8Params p{xq_ws, qw, sx_ws, sw, bias, out, nullptr, M, N, K, out_pitch(N, epilogue), epilogue};
@@ -345,7 +354,7 @@ int slim_int8_linear_colsplit(const void* x, int x_dtype, const int8_t* qw, cons
   if (!aligned16(x)) return fail(SLIM_ERR_ALIGN, "x must be 16-byte aligned");
   if ((rc = check_arch()) != SLIM_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = launch_bfly_rotate_quant(x, x_dtype, M, static_cast<int>(K), xq_ws, sx_ws, nullptr, st);
+  cudaError_t e = launch_act_quant(x, x_dtype, M, static_cast<int>(K), xq_ws, sx_ws, st);
   if (e != cudaSuccess) return cuda_fail(e, "activation quant launch");
   note_launch();
   GemmI8Params p{xq_ws, qw, sx_ws, sw, bias, outs[0], nullptr, M, N, K, ldo, epilogue};

@@ -33,9 +33,14 @@
 //    (about one per row) and a second block barrier combines them with A0.
 // 3. Codes. With r16 = fl(1 / (16 scale)), rint(S' r16) equals the reference's code unless
 //    S' r16 lies within 2^-13 + D r16 of a half-integer (2^-13 covers the reciprocal and the
-//    reference's division rounding). Such outputs of exact groups take the IEEE division; those
-//    of the other groups get a provisional code and go to a per-warp queue, which is drained one
-//    output per lane, reading the inputs from global memory and overwriting the provisional code.
+//    reference's division rounding). Such outputs of exact groups take the IEEE division.
+// Chains run on warps of their own (the fixers), behind the others (the streamers), so
+// no streamer waits for one: a streamer that finds the maximum uncertain writes provisional
+// codes against an interval [s_lo, s_hi] that contains the scale (an output's code is certain
+// when it is the same for every scale in it) and lists the candidates for the maximum; outputs
+// whose code is not certain are listed too. The fixer runs the listed chains from the staged
+// row in shared memory, one output per lane, settles the scale and overwrites the provisional
+// codes, then reuses the row's buffer.
 // A chain evaluates chunks 0..c0-1 in four independent partial sums (exact in any order) and
 // only chunks c0..15 as the reference's sequential chain.
 //
@@ -49,11 +54,6 @@
 #include "slim_ptx.cuh"
 
 namespace slim {
-
-// Queue entry key: (iteration of the CTA's row loop) << 18 | c0 << 14 | column (K <= 16384); the
-// row is blockIdx.x + it * gridDim.x, so rows per CTA are limited to 2^14.
-constexpr int kCertColBits = 14;
-constexpr int64_t kCertMaxIters = int64_t{1} << 14;
 
 template <int DT>
 struct CertFmt {
@@ -88,46 +88,96 @@ __device__ __forceinline__ void cert_load16(const unsigned char* p, float (&f)[1
   }
 }
 
-// The reference chain for output j of one group (grp = its 256 inputs, c0 as in step 1):
-// S_ref = fl-chain of sum_k sign(j, k) x_k over k = 0..255, sign(j, k) = sig(b) lam(l) for
-// k = 16 b + l. Chunks below c0 are summed exactly as four interleaved partial sums (every
-// partial sum there is exact, so the grouping cannot change it); from chunk c0 on the
-// accumulator is carried as sig(b) * acc, so every step is fma(x, lam_l, acc) with an exact
-// product and a chunk change multiplies it by sig(b) sig(b-1) = +-1 (rounding to nearest is
-// symmetric, so the carried chain rounds exactly like the plain one).
+// Two chain steps on one packed word of two bf16 (f16) inputs: acc = fl(fl(acc + l0 x0) + l1 x1)
+// with l0, l1 = +-1 packed the same way. The mixed-precision fma takes the 16-bit inputs as they
+// are stored (their product with +-1 is exact in fp32) and rounds once, like the fp32 chain.
 template <int DT>
-__device__ __noinline__ float cert_chain(const unsigned char* grp, int j, int c0) {
+__device__ __forceinline__ float cert_fma_pair(float acc, uint32_t w, uint32_t lp) {
+  if (DT == kBF16) {
+    asm("{\n\t.reg .b16 xl, xh, ll, lh;\n\t"
+        "mov.b32 {xl, xh}, %1;\n\t"
+        "mov.b32 {ll, lh}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, xl, ll, %0;\n\t"
+        "fma.rn.f32.bf16 %0, xh, lh, %0;\n\t}"
+        : "+f"(acc) : "r"(w), "r"(lp));
+  } else {
+    asm("{\n\t.reg .b16 xl, xh, ll, lh;\n\t"
+        "mov.b32 {xl, xh}, %1;\n\t"
+        "mov.b32 {ll, lh}, %2;\n\t"
+        "fma.rn.f32.f16 %0, xl, ll, %0;\n\t"
+        "fma.rn.f32.f16 %0, xh, lh, %0;\n\t}"
+        : "+f"(acc) : "r"(w), "r"(lp));
+  }
+  return acc;
+}
+
+// The sixteen chain steps of one chunk: 16-bit inputs through cert_fma_pair (lp = the signs
+// packed per input pair), fp32 inputs through fp32 fmas (lam).
+template <int DT>
+__device__ __forceinline__ float cert_chunk_steps(float acc, const uint4* q, const uint32_t (&lp)[8],
+                                                  const float (&lam)[16]) {
+  if (DT == kF32) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 u = q[i];
+      acc = __fmaf_rn(__uint_as_float(u.x), lam[4 * i], acc);
+      acc = __fmaf_rn(__uint_as_float(u.y), lam[4 * i + 1], acc);
+      acc = __fmaf_rn(__uint_as_float(u.z), lam[4 * i + 2], acc);
+      acc = __fmaf_rn(__uint_as_float(u.w), lam[4 * i + 3], acc);
+    }
+  } else {
+    const uint4 u0 = q[0], u1 = q[1];
+    acc = cert_fma_pair<DT>(acc, u0.x, lp[0]);
+    acc = cert_fma_pair<DT>(acc, u0.y, lp[1]);
+    acc = cert_fma_pair<DT>(acc, u0.z, lp[2]);
+    acc = cert_fma_pair<DT>(acc, u0.w, lp[3]);
+    acc = cert_fma_pair<DT>(acc, u1.x, lp[4]);
+    acc = cert_fma_pair<DT>(acc, u1.y, lp[5]);
+    acc = cert_fma_pair<DT>(acc, u1.z, lp[6]);
+    acc = cert_fma_pair<DT>(acc, u1.w, lp[7]);
+  }
+  return acc;
+}
+
+// The reference chain for output j of one group (grp = its 256 inputs in shared memory, c0 as in
+// step 1): S_ref = fl-chain of sum_k sign(j, k) x_k over k = 0..255, sign(j, k) = sig(b) lam(l)
+// for k = 16 b + l. Chunks below c0 are summed exactly, two at a time (any grouping is exact
+// there). From chunk c0 on the accumulator is carried as sig(b) * acc, so every step is
+// fma(x, lam_l, acc) with an exact product and a chunk change multiplies it by sig(b) sig(b-1)
+// = +-1 (rounding to nearest is symmetric, so the carried chain rounds exactly like the plain
+// one).
+template <int DT>
+__device__ __forceinline__ float cert_chain(const unsigned char* grp, int j, int c0) {
   const int j0 = j & 3, j1 = (j >> 2) & 3, j2 = (j >> 4) & 3, j3 = (j >> 6) & 3;
   float lam[16];
+  uint32_t lp[8];
+  const uint32_t one = DT == kF16 ? 0x3c00u : 0x3f80u;  // 1.0 in the 16-bit format; | 0x8000 = -1.0
 #pragma unroll
   for (int l = 0; l < 16; ++l) lam[l] = h4sign(j1, l >> 2) * h4sign(j0, l & 3);
-  constexpr int kEsz = CertFmt<DT>::kEsz;
-  float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  for (int b0 = 0; b0 < c0; b0 += 4) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int b = b0 + u;
-      if (b < c0) {
-        float f[16];
-        cert_load16<DT>(grp + 16 * b * kEsz, f);
-        float t = 0.0f;
-#pragma unroll
-        for (int l = 0; l < 16; ++l) t = __fmaf_rn(f[l], lam[l], t);
-        part[u] = __fmaf_rn(t, h4sign(j3, b >> 2) * h4sign(j2, b & 3), part[u]);
-      }
-    }
+  for (int e = 0; e < 8; ++e)
+    lp[e] = (one | (lam[2 * e] < 0.0f ? 0x8000u : 0u)) | ((one | (lam[2 * e + 1] < 0.0f ? 0x8000u : 0u)) << 16);
+  constexpr int kChunk = 16 * CertFmt<DT>::kEsz;
+  float pa = 0.0f, pb = 0.0f;
+  int b = 0;
+  for (; b + 2 <= c0; b += 2) {
+    const float ta = cert_chunk_steps<DT>(0.0f, reinterpret_cast<const uint4*>(grp + b * kChunk), lp, lam);
+    const float tb = cert_chunk_steps<DT>(0.0f, reinterpret_cast<const uint4*>(grp + (b + 1) * kChunk), lp, lam);
+    pa = __fmaf_rn(ta, h4sign(j3, b >> 2) * h4sign(j2, b & 3), pa);
+    pb = __fmaf_rn(tb, h4sign(j3, (b + 1) >> 2) * h4sign(j2, (b + 1) & 3), pb);
   }
-  const float pre = (part[0] + part[1]) + (part[2] + part[3]);
+  if (b < c0) {
+    const float ta = cert_chunk_steps<DT>(0.0f, reinterpret_cast<const uint4*>(grp + b * kChunk), lp, lam);
+    pa = __fmaf_rn(ta, h4sign(j3, b >> 2) * h4sign(j2, b & 3), pa);
+  }
+  const float pre = pa + pb;
   if (c0 >= 16) return pre;
   float sig_prev = h4sign(j3, c0 >> 2) * h4sign(j2, c0 & 3);
   float acc = pre * sig_prev;
-  for (int b = c0; b < 16; ++b) {
-    float f[16];
-    cert_load16<DT>(grp + 16 * b * kEsz, f);
+  for (b = c0; b < 16; ++b) {
     const float sig = h4sign(j3, b >> 2) * h4sign(j2, b & 3);
     acc *= sig * sig_prev;
-#pragma unroll
-    for (int l = 0; l < 16; ++l) acc = __fmaf_rn(f[l], lam[l], acc);
+    acc = cert_chunk_steps<DT>(acc, reinterpret_cast<const uint4*>(grp + b * kChunk), lp, lam);
     sig_prev = sig;
   }
   return acc * sig_prev;
@@ -160,26 +210,6 @@ __device__ __forceinline__ uint32_t cert_quant_pair(float2 S, float2 r2, float2&
   return __byte_perm(__float_as_uint(xq.x), __float_as_uint(xq.y), 0x0040);
 }
 
-// One lane per queued output: run its chain from global memory and overwrite the provisional
-// code. The warp's entries [0, n) are read; every lane of the warp must call this.
-template <int DT>
-__device__ __forceinline__ void cert_drain(const unsigned char* src, int K, int8_t* q_out, const uint32_t* qkey,
-                                           const float* qscale, int n, int lane) {
-  __syncwarp();
-  if (lane < n) {
-    constexpr int kEsz = CertFmt<DT>::kEsz;
-    const uint32_t key = qkey[lane];
-    const int64_t row = blockIdx.x + static_cast<int64_t>(key >> 18) * gridDim.x;
-    const uint32_t col = key & ((1u << kCertColBits) - 1u);
-    const int c0 = static_cast<int>((key >> kCertColBits) & 15u);
-    const float scale = qscale[lane];
-    const int64_t e0 = row * K + (col & ~255u);
-    const float S = cert_chain<DT>(src + e0 * kEsz, static_cast<int>(col & 255u), c0);
-    q_out[row * K + col] = quant_code(__fmul_rn(S, 0.0625f), scale);
-  }
-  __syncwarp();
-}
-
 // Group bound of step 1 from a half-warp's chunk sums (l1 = sum |x| of this thread's chunk) and
 // chunk minima: D (0 for an exact group) and c0 (16 when exact). r = chunk index; every lane of
 // the warp calls this (the two half-warps hold different groups).
@@ -209,31 +239,99 @@ __device__ __forceinline__ float cert_group_bound(float l1, float mn, int r, int
   return __fmaf_ru(d, 1.0009765625f, 7.52316385e-37f);          // (1 + 2^-10), + 2^-120
 }
 
-// Block barrier over the CTA's warps (mbarrier `cbar`, one arrival per warp) that does useful work
-// while it waits: a warp whose arrival does not complete the phase drains its own queue of
-// outputs awaiting their chain (if it holds at least `qmin`) before waiting. Every wait is
-// bounded; returns false on a timeout (error recorded).
-template <int DT>
-__device__ __forceinline__ bool cert_cta_sync(uint64_t* cbar, uint32_t& parity, int lane, const unsigned char* src,
-                                              int K, int8_t* q_out, const uint32_t* qkey, const float* qscale,
-                                              int& qn, int qmin) {
+// Provisional codes of a thread's 16 output pairs into the transpose buffer (code of output
+// 16 rr + r at cbuf[16 rr + r], group p in the low byte), and the mask of outputs whose code is
+// not certain: |S' rm - code| (+ |S'| w when the scale is an interval) above lim.
+template <bool kInterval>
+__device__ __forceinline__ uint32_t cert_codes(const float2 (&v)[16], float rm, float w, float lim_a, float lim_b,
+                                               uint16_t* cbuf, int r) {
+  const float2 r2 = make_float2(rm, rm);
+  uint32_t near = 0;
+#pragma unroll
+  for (int rr = 0; rr < 16; ++rr) {
+    float2 d;
+    cbuf[16 * rr + r] = static_cast<uint16_t>(cert_quant_pair(v[rr], r2, d));
+    if (kInterval) {
+      d.x = __fmaf_ru(fabsf(v[rr].x), w, d.x);
+      d.y = __fmaf_ru(fabsf(v[rr].y), w, d.y);
+    }
+    if (d.x > lim_a) near |= 1u << rr;
+    if (d.y > lim_b) near |= 1u << (16 + rr);
+  }
+  return near;
+}
+
+// ------------------------------------------------------------------ the kernel
+// Per staged row: a record and two lists (columns of the outputs whose chain is needed), filled by
+// the streamer warps and settled by the fixer warp that owns the row's buffer.
+struct CertRec {
+  uint32_t ncand;     // candidates for the row maximum (uncertain rows only)
+  uint32_t nties;     // outputs whose code waits for its chain
+  uint32_t flags;     // kCertUnsure: the scale is settled by the fixer; kCertOverflow: a list overflowed
+  float a0;           // exact part of the row maximum (S units)
+  float scale;        // the row scale (certain rows)
+  uint32_t pad[3];
+};
+constexpr uint32_t kCertUnsure = 1u, kCertOverflow = 2u;
+constexpr int kCertCand = 64;   // candidate list length per row
+constexpr int kCertTies = 512;  // near-tie list length per row
+
+// Shared-memory layout (bytes): mbarriers full[2] (row staged), done[2] (streamers finished a
+// row), cbar (streamer block barrier); failure flag; warp partials; records; per-group c0; lists;
+// then the two staged rows and the streamers' transpose buffers.
+constexpr int kCertOffFull = 0, kCertOffDone = 16, kCertOffCbar = 32, kCertOffFail = 40, kCertOffRed = 48;
+constexpr int kCertOffRec = 432, kCertOffC0 = 496, kCertOffCand = 624, kCertOffTies = 880, kCertOffRows = 2944;
+
+// Appends this lane's outputs (mask bits: bit i < 16 -> group p, else group p + G2; output
+// 16 (i & 15) + r) to a row list with one atomic per warp; on overflow flags the record instead.
+__device__ __forceinline__ void cert_append(uint32_t mask, int p, int G2, int r, int lane, uint16_t* list,
+                                            uint32_t* count, uint32_t cap, uint32_t* flags) {
+  if (!__any_sync(0xffffffffu, mask != 0u)) return;
+  const int n = __popc(mask);
+  int incl = n;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += u;
+  }
+  const int total = __shfl_sync(0xffffffffu, incl, 31);
+  uint32_t base = 0;
+  if (lane == 0) base = atomicAdd(count, static_cast<uint32_t>(total));
+  base = __shfl_sync(0xffffffffu, base, 0);
+  if (base + static_cast<uint32_t>(total) > cap) {
+    if (lane == 0) atomicOr(flags, kCertOverflow);
+    return;
+  }
+  uint32_t k = base + static_cast<uint32_t>(incl - n);
+  while (mask != 0u) {
+    const int bit = __ffs(mask) - 1;
+    mask &= mask - 1u;
+    list[k++] = static_cast<uint16_t>((bit < 16 ? p : p + G2) * 256 + 16 * (bit & 15) + r);
+  }
+}
+
+// Block barrier of the streamer warps (mbarrier, one arrival per warp, bounded wait).
+__device__ __forceinline__ bool cert_streamer_sync(uint64_t* cbar, uint32_t& parity, int lane) {
   __syncwarp();
   if (lane == 0) mbar_arrive(cbar);
-  const bool done = __any_sync(0xffffffffu, mbar_try_wait(cbar, parity));
-  if (!done && qn >= qmin) {
-    cert_drain<DT>(src, K, q_out, qkey, qscale, qn, lane);
-    qn = 0;
-  }
   const bool ok = mbar_wait(cbar, parity, kErrWaitTimeoutEpilogue);
   parity ^= 1u;
   return __all_sync(0xffffffffu, ok);
 }
 
-// Persistent over rows, as bfly2_rotate_quant_kernel: a row of G groups is split into G2 =
-// ceil(G/2) group pairs (g, g + G2), 16 threads per pair; thread (p, r) holds chunk r (16
-// consecutive inputs) of both groups as the two lanes of packed fp32x2 registers. Rows arrive
-// in shared memory by double-buffered bulk copies.
-template <int DT, int MAXR, int QN>
+// Row scale from the maximum in S units (slimdit/int8.py:49: max(fl(absmax / 127), 1e-30)).
+__device__ __forceinline__ float cert_scale(float absmax_s) { return row_scale_from_absmax(__fmul_rn(absmax_s, 0.0625f)); }
+
+// Persistent over rows. Streamer warps (all but the last NF): a row of G groups is split into
+// G2 = ceil(G/2) group pairs (g, g + G2), 16 threads per pair; thread (p, r) holds chunk r (16
+// consecutive inputs) of both groups as the two lanes of packed fp32x2 registers. They compute
+// S', the certificates, the row maximum bounds, the scale (or, when the maximum is uncertain, an
+// interval that contains it), provisional codes, and list the outputs whose chain is needed.
+// NF fixer warps (the last ones) follow the streamers: a fixer runs the listed chains of a row
+// from its staging buffer in shared memory (one output per lane), settles the row's scale and
+// codes, and then reuses the buffer for the row after next. Rows arrive by bulk copies, two
+// buffers; with two fixers each owns one buffer.
+template <int DT, int MAXR, int NF>
 __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restrict__ x, int64_t rows, int K,
                                                            int8_t* __restrict__ q_out,
                                                            float* __restrict__ scale_out) {
@@ -242,270 +340,270 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
   const uint32_t row_bytes = static_cast<uint32_t>(K) * kEsz;
   const int t = threadIdx.x;
   const int warp = t >> 5, lane = t & 31;
-  const int nw = blockDim.x >> 5;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);           // 2 row-staging mbarriers, cbar
-  uint64_t* cbar = bar + 2;                                        // block barrier (one arrival per warp)
-  volatile uint32_t* fail_flag = reinterpret_cast<volatile uint32_t*>(smem_raw + 24);  // a staged row never arrived
-  float* red = reinterpret_cast<float*>(smem_raw + 32);              // [2 parities][4 kinds][16 warps]
-  uint32_t* qkey_all = reinterpret_cast<uint32_t*>(smem_raw + 544);  // [warps][QN] queued outputs
-  float* qscale_all = reinterpret_cast<float*>(qkey_all + nw * QN);  // [warps][QN] their row scales
-  unsigned char* rowbuf = reinterpret_cast<unsigned char*>(qscale_all + nw * QN);  // 2 staged rows
+  const int ns = (blockDim.x >> 5) - NF;  // streamer warps; the last NF warps are the fixers
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kCertOffFull);
+  uint64_t* done = reinterpret_cast<uint64_t*>(smem_raw + kCertOffDone);
+  uint64_t* cbar = reinterpret_cast<uint64_t*>(smem_raw + kCertOffCbar);
+  volatile uint32_t* fail_flag = reinterpret_cast<volatile uint32_t*>(smem_raw + kCertOffFail);
+  float* red = reinterpret_cast<float*>(smem_raw + kCertOffRed);  // [2 parities][3 kinds][16 warps]
+  CertRec* recs = reinterpret_cast<CertRec*>(smem_raw + kCertOffRec);
+  uint8_t* c0tabs = smem_raw + kCertOffC0;                           // [2][64]
+  uint16_t* cands = reinterpret_cast<uint16_t*>(smem_raw + kCertOffCand);  // [2][kCertCand]
+  uint16_t* ties = reinterpret_cast<uint16_t*>(smem_raw + kCertOffTies);   // [2][kCertTies]
+  unsigned char* rowbuf = smem_raw + kCertOffRows;                   // 2 staged rows
   float2* xbuf = reinterpret_cast<float2*>(rowbuf + 2 * static_cast<size_t>(row_bytes));
-  uint32_t* qkey = qkey_all + warp * QN;
-  float* qscale = qscale_all + warp * QN;
-
+  const unsigned char* src = static_cast<const unsigned char*>(x);
   const int G = K >> 8;
   const int G2 = (G + 1) >> 1;
-  const int p = t >> 4;  // group pair
-  const int r = t & 15;  // chunk within the group
-  const bool act_a = p < G2;
-  const bool act_b = p + G2 < G;
-  float2* gbuf = xbuf + (warp * 2 + ((lane >> 4) & 1)) * 256;
-  const unsigned char* src = static_cast<const unsigned char*>(x);
-  int qn = 0;  // queued outputs of this warp (warp-uniform)
 
   if (t == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
-    mbar_init(cbar, static_cast<uint32_t>(nw));
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    mbar_init(&done[0], static_cast<uint32_t>(ns));
+    mbar_init(&done[1], static_cast<uint32_t>(ns));
+    mbar_init(cbar, static_cast<uint32_t>(ns));
     *fail_flag = 0u;
+    for (int b = 0; b < 2; ++b) {
+      recs[b].ncand = 0u;
+      recs[b].nties = 0u;
+      recs[b].flags = 0u;
+    }
     fence_mbar_init();
   }
   __syncthreads();
-  int64_t row = blockIdx.x;
-  uint32_t pending = 0, pending_parity = 0;
   if (t == 0) {
     for (int b = 0; b < 2; ++b) {
-      const int64_t rb = row + b * static_cast<int64_t>(gridDim.x);
+      const int64_t rb = blockIdx.x + b * static_cast<int64_t>(gridDim.x);
       if (rb < rows) {
-        mbar_arrive_expect_tx(&bar[b], row_bytes);
-        bulk_load(rowbuf + b * row_bytes, src + rb * row_bytes, row_bytes, &bar[b]);
-        pending |= 1u << b;
+        mbar_arrive_expect_tx(&full[b], row_bytes);
+        bulk_load(rowbuf + b * row_bytes, src + rb * row_bytes, row_bytes, &full[b]);
       }
     }
   }
-  bool failed = false;
-  uint32_t cparity = 0;                // phase parity of cbar
-  const int qmin = QN / 4;             // smallest queue worth draining while waiting
-  for (int it = 0; row < rows; row += gridDim.x, ++it) {
-    const int b = it & 1;
-    const bool ok = mbar_wait(&bar[b], (it >> 1) & 1, kErrWaitTimeoutProducer);
-    if (ok && t == 0) pending &= ~(1u << b);
-    if (!ok) *fail_flag = 1u;  // seen by every thread after the next block barrier
-    const unsigned char* stage = rowbuf + b * row_bytes;
-    const int ea = p * 256 + 16 * r;  // element offset of chunk a in the row
-    const int eb = ea + G2 * 256;     // chunk b
-    float2 v[16];
-    float l1a = 0.0f, l1b = 0.0f, mna = __uint_as_float(0x7f800000u), mnb = __uint_as_float(0x7f800000u);
-    if (act_a) {
-      float fa[16], fb[16];
-      cert_load16<DT>(stage + ea * kEsz, fa);
-      if (act_b) {
-        cert_load16<DT>(stage + eb * kEsz, fb);
-      } else {
+
+  if (warp < ns) {
+    // ------------------------------------------------------------ streamers
+    const int p = t >> 4;  // group pair
+    const int r = t & 15;  // chunk within the group
+    const bool act_a = p < G2;
+    const bool act_b = p + G2 < G;
+    float2* gbuf = xbuf + (warp * 2 + ((lane >> 4) & 1)) * 256;
+    uint32_t cparity = 0;
+    int64_t row = blockIdx.x;
+    for (int it = 0; row < rows; row += gridDim.x, ++it) {
+      const int b = it & 1;
+      if (!mbar_wait(&full[b], (it >> 1) & 1, kErrWaitTimeoutProducer)) *fail_flag = 1u;
+      CertRec* rc = recs + b;
+      const unsigned char* stage = rowbuf + b * row_bytes;
+      const int ea = p * 256 + 16 * r;  // element offset of chunk a in the row
+      const int eb = ea + G2 * 256;     // chunk b
+      float2 v[16];
+      float l1a = 0.0f, l1b = 0.0f, mna = __uint_as_float(0x7f800000u), mnb = __uint_as_float(0x7f800000u);
+      if (act_a) {
+        float fa[16], fb[16];
+        cert_load16<DT>(stage + ea * kEsz, fa);
+        if (act_b) {
+          cert_load16<DT>(stage + eb * kEsz, fb);
+        } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) fb[i] = 0.0f;
+          for (int i = 0; i < 16; ++i) fb[i] = 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          l1a += fabsf(fa[i]);
+          l1b += fabsf(fb[i]);
+          mna = fminf(mna, fabsf(fa[i]));
+          mnb = fminf(mnb, fabsf(fb[i]));
+          v[i] = make_float2(fa[i], fb[i]);
+        }
+        bfly16x2(v);  // digits 0, 1
+#pragma unroll
+        for (int i = 0; i < 16; i += 2)
+          *reinterpret_cast<float4*>(gbuf + xpos2(r, i)) = make_float4(v[i].x, v[i].y, v[i + 1].x, v[i + 1].y);
       }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        l1a += fabsf(fa[i]);
-        l1b += fabsf(fb[i]);
-        mna = fminf(mna, fabsf(fa[i]));
-        mnb = fminf(mnb, fabsf(fb[i]));
-        v[i] = make_float2(fa[i], fb[i]);
+      int c0a, c0b;
+      float Da = cert_group_bound<DT>(l1a, mna, r, lane, c0a);
+      float Db = cert_group_bound<DT>(l1b, mnb, r, lane, c0b);
+      if (!act_a) Da = 0.0f;
+      if (!act_b) Db = 0.0f;
+      if (r == 0) {
+        if (act_a) c0tabs[b * 64 + p] = static_cast<uint8_t>(c0a);
+        if (act_b) c0tabs[b * 64 + p + G2] = static_cast<uint8_t>(c0b);
       }
-      bfly16x2(v);  // digits 0, 1
+      __syncwarp();
+      float ama = 0.0f, amb = 0.0f;
+      if (act_a) {
 #pragma unroll
-      for (int i = 0; i < 16; i += 2)
-        *reinterpret_cast<float4*>(gbuf + xpos2(r, i)) = make_float4(v[i].x, v[i].y, v[i + 1].x, v[i + 1].y);
+        for (int rr = 0; rr < 16; ++rr) v[rr] = gbuf[xpos2(rr, r)];
+        bfly16x2(v);  // digits 2, 3: lanes hold S' for outputs 16 rr + r of groups p and p + G2
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr) {
+          ama = fmaxf(ama, fabsf(v[rr].x));
+          amb = fmaxf(amb, fabsf(v[rr].y));
+        }
+      }
+      {  // row maximum bounds: one redux per kind and warp, one barrier of the streamers
+        const float tA0 = fmaxf(Da == 0.0f ? ama : 0.0f, Db == 0.0f ? amb : 0.0f);
+        const float tA = fmaxf(fmaxf(__fsub_rd(ama, Da), __fsub_rd(amb, Db)), 0.0f);
+        const float tB = fmaxf(Da > 0.0f ? __fadd_ru(ama, Da) : 0.0f, Db > 0.0f ? __fadd_ru(amb, Db) : 0.0f);
+        const unsigned w0 = __reduce_max_sync(0xffffffffu, __float_as_uint(tA0));
+        const unsigned w1 = __reduce_max_sync(0xffffffffu, __float_as_uint(tA));
+        const unsigned w2 = __reduce_max_sync(0xffffffffu, __float_as_uint(tB));
+        if (lane == 0) {
+          red[(b * 3 + 0) * 16 + warp] = __uint_as_float(w0);
+          red[(b * 3 + 1) * 16 + warp] = __uint_as_float(w1);
+          red[(b * 3 + 2) * 16 + warp] = __uint_as_float(w2);
+        }
+      }
+      if (!cert_streamer_sync(cbar, cparity, lane) || *fail_flag != 0u) break;  // error recorded
+      const float A0 = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < ns ? __float_as_uint(red[(b * 3 + 0) * 16 + lane]) : 0u));
+      const float A = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < ns ? __float_as_uint(red[(b * 3 + 1) * 16 + lane]) : 0u));
+      const float B = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < ns ? __float_as_uint(red[(b * 3 + 2) * 16 + lane]) : 0u));
+      // the scale, or (maximum uncertain) an interval [s_lo, s_hi] that contains it; codes are
+      // taken from S' rm, and an output's code is certain unless S' rm lies within
+      // 2^-13 + D r_hi + |S'| w of a half-integer (w covers the interval; 0 for a certain scale)
+      const bool unsure = B >= A && B > 0.0f;
+      const float top = unsure ? fmaxf(A0, B) : A0;
+      const float scale = cert_scale(unsure ? A : A0);  // s_lo when unsure (provisional codes)
+      const float rm = __frcp_rn(__fmul_rn(16.0f, scale));
+      float w = 0.0f;
+      if (unsure)
+        w = __fmaf_ru(rm, 2.384185791015625e-07f,
+                      __fsub_ru(__frcp_ru(__fmul_rn(16.0f, scale)), __frcp_rd(__fmul_rn(16.0f, cert_scale(top)))));
+      const bool tiny_row = top < 8.271806125530277e-25f;  // 2^-80: S / 16 could be subnormal
+      if (t == 0) {
+        rc->a0 = A0;
+        rc->scale = scale;
+        if (unsure) atomicOr(&rc->flags, kCertUnsure);
+        else scale_out[row] = scale;
+      }
+      const int64_t rbase = row * static_cast<int64_t>(K);
+      uint32_t near = 0, cand = 0;  // bit rr: group p, bit 16 + rr: group p + G2
+      __syncwarp();
+      uint16_t* cbuf = reinterpret_cast<uint16_t*>(gbuf);
+      if (act_a) {
+        const float lim_a = __fsub_rd(0.5f, __fmaf_ru(Da, __fmul_ru(rm, 1.0009765625f), 1.220703125e-4f));
+        const float lim_b = __fsub_rd(0.5f, __fmaf_ru(Db, __fmul_ru(rm, 1.0009765625f), 1.220703125e-4f));
+        near = unsure ? cert_codes<true>(v, rm, w, lim_a, lim_b, cbuf, r) : cert_codes<false>(v, rm, w, lim_a, lim_b, cbuf, r);
+        if (tiny_row) near = ~0u;
+        if (!act_b) near &= 0xffffu;
+        if (unsure) {
+#pragma unroll
+          for (int rr = 0; rr < 16; ++rr) {
+            if (Da > 0.0f && __fadd_ru(fabsf(v[rr].x), Da) >= A) cand |= 1u << rr;
+            if (Db > 0.0f && __fadd_ru(fabsf(v[rr].y), Db) >= A) cand |= 1u << (16 + rr);
+          }
+        } else {
+          // exact groups with a certain scale: S' = S_ref, the IEEE division settles the code here
+          uint32_t ex = near & ~((Da > 0.0f ? 0x0000ffffu : 0u) | (Db > 0.0f ? 0xffff0000u : 0u));
+          near &= ~ex;
+          while (ex != 0u) {
+            const int bit = __ffs(ex) - 1;
+            ex &= ex - 1u;
+            const int rr = bit & 15;
+            float sv = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (i == rr) sv = bit < 16 ? v[i].x : v[i].y;
+            const uint8_t c = static_cast<uint8_t>(quant_code(__fmul_rn(sv, 0.0625f), scale));
+            const uint16_t cw = cbuf[16 * rr + r];
+            cbuf[16 * rr + r] = bit < 16 ? static_cast<uint16_t>((cw & 0xff00u) | c)
+                                         : static_cast<uint16_t>((cw & 0x00ffu) | (static_cast<uint32_t>(c) << 8));
+          }
+        }
+      }
+      __syncwarp();
+      if (act_a) {
+        const uint4* c4 = reinterpret_cast<const uint4*>(cbuf + 16 * r);
+        const uint4 u0 = c4[0], u1 = c4[1];  // 16 (a, b) byte pairs of chunk r
+        uint4 oa, ob;
+        oa.x = __byte_perm(u0.x, u0.y, 0x6420); ob.x = __byte_perm(u0.x, u0.y, 0x7531);
+        oa.y = __byte_perm(u0.z, u0.w, 0x6420); ob.y = __byte_perm(u0.z, u0.w, 0x7531);
+        oa.z = __byte_perm(u1.x, u1.y, 0x6420); ob.z = __byte_perm(u1.x, u1.y, 0x7531);
+        oa.w = __byte_perm(u1.z, u1.w, 0x6420); ob.w = __byte_perm(u1.z, u1.w, 0x7531);
+        *reinterpret_cast<uint4*>(q_out + rbase + ea) = oa;
+        if (act_b) *reinterpret_cast<uint4*>(q_out + rbase + eb) = ob;
+      }
+      cert_append(cand, p, G2, r, lane, cands + b * kCertCand, &rc->ncand, kCertCand, &rc->flags);
+      cert_append(near, p, G2, r, lane, ties + b * kCertTies, &rc->nties, kCertTies, &rc->flags);
+      // provisional codes and lists complete before the fixer takes the row
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&done[b]);
     }
-    // per group: D and c0 from the chunk prefix sums of the 16 chunk owners (half-warp)
-    int c0a, c0b;
-    float Da = cert_group_bound<DT>(l1a, mna, r, lane, c0a);
-    float Db = cert_group_bound<DT>(l1b, mnb, r, lane, c0b);
-    if (!act_a) Da = 0.0f;
-    if (!act_b) Db = 0.0f;
-    __syncwarp();
-    float ama = 0.0f, amb = 0.0f;
-    if (act_a) {
-#pragma unroll
-      for (int rr = 0; rr < 16; ++rr) v[rr] = gbuf[xpos2(rr, r)];
-      bfly16x2(v);  // digits 2, 3: lanes hold S' for outputs 16 rr + r of groups p and p + G2
-#pragma unroll
-      for (int rr = 0; rr < 16; ++rr) {
-        ama = fmaxf(ama, fabsf(v[rr].x));
-        amb = fmaxf(amb, fabsf(v[rr].y));
+  } else {
+    // ------------------------------------------------------------ fixers
+    // Fixer f takes the rows of iterations f, f + NF, ... (with two fixers, fixer f owns buffer
+    // f). Per row, two phases over listed columns, one output per lane, one chain code path:
+    //   phase 0: the maximum (uncertain rows: the candidates; overflowed rows: every output),
+    //   phase 1: the codes (the listed near-tie outputs; overflowed rows: every output).
+    for (int it = warp - ns; blockIdx.x + static_cast<int64_t>(it) * gridDim.x < rows; it += NF) {
+      const int b = it & 1;
+      const int64_t row = blockIdx.x + static_cast<int64_t>(it) * gridDim.x;
+      if (!mbar_wait(&done[b], (it >> 1) & 1, kErrWaitTimeoutDrain)) break;  // streamers stopped
+      CertRec* rc = recs + b;
+      unsigned char* buf = rowbuf + b * row_bytes;
+      const uint8_t* c0tab = c0tabs + b * 64;
+      const uint32_t flags = rc->flags;
+      const bool all = (flags & kCertOverflow) != 0u;
+      const int64_t rbase = row * static_cast<int64_t>(K);
+      float scale = rc->scale;
+      float m = rc->a0;
+      for (int phase = (all || (flags & kCertUnsure)) ? 0 : 1; phase < 2; ++phase) {
+        const int n = all ? K : static_cast<int>(phase == 0 ? rc->ncand : rc->nties);
+        const uint16_t* list = phase == 0 ? cands + b * kCertCand : ties + b * kCertTies;
+        for (int e = lane; e < n; e += 32) {
+          const int col = all ? e : list[e];
+          const float S = cert_chain<DT>(buf + (col & ~255) * kEsz, col & 255, c0tab[col >> 8]);
+          if (phase == 0) m = fmaxf(m, fabsf(S));
+          else q_out[rbase + col] = quant_code(__fmul_rn(S, 0.0625f), scale);
+        }
+        if (phase == 0) {
+          m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
+          scale = cert_scale(m);
+          if (lane == 0) scale_out[row] = scale;
+        }
       }
-    }
-    // row maximum bounds: one redux per kind and warp, one block barrier
-    {
-      const float tA0 = fmaxf(Da == 0.0f ? ama : 0.0f, Db == 0.0f ? amb : 0.0f);
-      const float tA = fmaxf(fmaxf(__fsub_rd(ama, Da), __fsub_rd(amb, Db)), 0.0f);
-      const float tB = fmaxf(Da > 0.0f ? __fadd_ru(ama, Da) : 0.0f, Db > 0.0f ? __fadd_ru(amb, Db) : 0.0f);
-      const unsigned w0 = __reduce_max_sync(0xffffffffu, __float_as_uint(tA0));
-      const unsigned w1 = __reduce_max_sync(0xffffffffu, __float_as_uint(tA));
-      const unsigned w2 = __reduce_max_sync(0xffffffffu, __float_as_uint(tB));
-      if (lane == 0) {
-        red[(b * 4 + 0) * 16 + warp] = __uint_as_float(w0);
-        red[(b * 4 + 1) * 16 + warp] = __uint_as_float(w1);
-        red[(b * 4 + 2) * 16 + warp] = __uint_as_float(w2);
-      }
-    }
-    if (!cert_cta_sync<DT>(cbar, cparity, lane, src, K, q_out, qkey, qscale, qn, qmin) || *fail_flag != 0u) {
-      failed = true;  // a staged row never arrived or a barrier timed out (error recorded)
-      break;
-    }
-    const float A0 = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < nw ? __float_as_uint(red[(b * 4 + 0) * 16 + lane]) : 0u));
-    const float A = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < nw ? __float_as_uint(red[(b * 4 + 1) * 16 + lane]) : 0u));
-    const float B = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < nw ? __float_as_uint(red[(b * 4 + 2) * 16 + lane]) : 0u));
-    float absmax_s = A0;
-    if (B >= A && B > 0.0f) {  // uniform: the maximum may sit in an inexact group
-      // candidates as a mask (bit rr: group p, bit 16 + rr: group p + G2), then one chain each
-      uint32_t cmask = 0;
-      if (act_a && Da > 0.0f && __fadd_ru(ama, Da) >= A) {
-#pragma unroll
-        for (int rr = 0; rr < 16; ++rr)
-          if (__fadd_ru(fabsf(v[rr].x), Da) >= A) cmask |= 1u << rr;
-      }
-      if (act_b && Db > 0.0f && __fadd_ru(amb, Db) >= A) {
-#pragma unroll
-        for (int rr = 0; rr < 16; ++rr)
-          if (__fadd_ru(fabsf(v[rr].y), Db) >= A) cmask |= 1u << (16 + rr);
-      }
-      float cm = 0.0f;
-      while (cmask != 0u) {
-        const int bit = __ffs(cmask) - 1;
-        cmask &= cmask - 1u;
-        const int grp = bit < 16 ? p : p + G2;
-        cm = fmaxf(cm, fabsf(cert_chain<DT>(stage + grp * 256 * kEsz, 16 * (bit & 15) + r, bit < 16 ? c0a : c0b)));
-      }
-      const unsigned wc = __reduce_max_sync(0xffffffffu, __float_as_uint(cm));
-      if (lane == 0) red[(b * 4 + 3) * 16 + warp] = __uint_as_float(wc);
-      if (!cert_cta_sync<DT>(cbar, cparity, lane, src, K, q_out, qkey, qscale, qn, qmin)) {
-        failed = true;
-        break;
-      }
-      const float cmax = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < nw ? __float_as_uint(red[(b * 4 + 3) * 16 + lane]) : 0u));
-      absmax_s = fmaxf(A0, cmax);
-    }
-    // every thread has read this row's stage: refill the buffer with the row after next
-    if (t == 0) {
-      const int64_t rn = row + 2 * static_cast<int64_t>(gridDim.x);
-      if (rn < rows) {
-        mbar_arrive_expect_tx(&bar[b], row_bytes);
-        bulk_load(rowbuf + b * row_bytes, src + rn * row_bytes, row_bytes, &bar[b]);
-        pending |= 1u << b;
-        pending_parity = (pending_parity & ~(1u << b)) | ((((it + 2) >> 1) & 1u) << b);
-      }
-    }
-    const float scale = row_scale_from_absmax(__fmul_rn(absmax_s, 0.0625f));
-    const float r16 = __frcp_rn(__fmul_rn(16.0f, scale));
-    const bool tiny_row = absmax_s < 8.271806125530277e-25f;  // 2^-80: S / 16 could be subnormal
-    if (t == 0) scale_out[row] = scale;
-    const int64_t rbase = row * static_cast<int64_t>(K);
-    // codes: provisional from S' r16, written to the transpose buffer; outputs near a rounding
-    // boundary are marked (bit rr: group p, bit 16 + rr: group p + G2) and settled below
-    uint32_t flags = 0;  // queued outputs (inexact groups)
-    __syncwarp();
-    uint16_t* cbuf = reinterpret_cast<uint16_t*>(gbuf);
-    if (act_a) {
-      const float2 r2 = make_float2(r16, r16);
-      const float lim_a = __fsub_rd(0.5f, __fmaf_ru(Da, __fmul_ru(r16, 1.0009765625f), 1.220703125e-4f));
-      const float lim_b = __fsub_rd(0.5f, __fmaf_ru(Db, __fmul_ru(r16, 1.0009765625f), 1.220703125e-4f));
-      uint32_t near = 0;
-#pragma unroll
-      for (int rr = 0; rr < 16; ++rr) {
-        float2 d;
-        cbuf[16 * rr + r] = static_cast<uint16_t>(cert_quant_pair(v[rr], r2, d));
-        if (d.x > lim_a) near |= 1u << rr;
-        if (d.y > lim_b) near |= 1u << (16 + rr);
-      }
-      if (tiny_row) near = ~0u;
-      if (!act_b) near &= 0xffffu;
-      // inexact groups: queued for their chain; exact groups: the IEEE division on S' = S_ref
-      flags = near & ((Da > 0.0f ? 0x0000ffffu : 0u) | (Db > 0.0f ? 0xffff0000u : 0u));
-      near &= ~flags;
-      while (near != 0u) {
-        const int bit = __ffs(near) - 1;
-        near &= near - 1u;
-        const int rr = bit & 15;
-        float sv = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (i == rr) sv = bit < 16 ? v[i].x : v[i].y;
-        const uint8_t c = static_cast<uint8_t>(quant_code(__fmul_rn(sv, 0.0625f), scale));
-        const uint16_t cw = cbuf[16 * rr + r];
-        cbuf[16 * rr + r] = bit < 16 ? static_cast<uint16_t>((cw & 0xff00u) | c)
-                                     : static_cast<uint16_t>((cw & 0x00ffu) | (static_cast<uint32_t>(c) << 8));
-      }
-    }
-    __syncwarp();
-    if (act_a) {
-      const uint4* c4 = reinterpret_cast<const uint4*>(cbuf + 16 * r);
-      const uint4 u0 = c4[0], u1 = c4[1];  // 16 (a, b) byte pairs of chunk r
-      uint4 oa, ob;
-      oa.x = __byte_perm(u0.x, u0.y, 0x6420); ob.x = __byte_perm(u0.x, u0.y, 0x7531);
-      oa.y = __byte_perm(u0.z, u0.w, 0x6420); ob.y = __byte_perm(u0.z, u0.w, 0x7531);
-      oa.z = __byte_perm(u1.x, u1.y, 0x6420); ob.z = __byte_perm(u1.x, u1.y, 0x7531);
-      oa.w = __byte_perm(u1.z, u1.w, 0x6420); ob.w = __byte_perm(u1.z, u1.w, 0x7531);
-      *reinterpret_cast<uint4*>(q_out + rbase + ea) = oa;
-      if (act_b) *reinterpret_cast<uint4*>(q_out + rbase + eb) = ob;
-    }
-    __syncwarp();  // provisional codes stored before any queued output overwrites its code
-    // each round, every lane offers its lowest queued output; at most the queue's free room is
-    // taken (the rest wait for the next round), and a full queue is drained at once
-    while (__any_sync(0xffffffffu, flags != 0u)) {
-      const int bit = flags != 0u ? __ffs(flags) - 1 : -1;
-      const unsigned ball = __ballot_sync(0xffffffffu, bit >= 0);
-      const int room = QN - qn;
-      const int rank = __popc(ball & ((1u << lane) - 1u));
-      if (bit >= 0 && rank < room) {
-        const int grp = bit < 16 ? p : p + G2;
-        const uint32_t c0 = static_cast<uint32_t>(bit < 16 ? c0a : c0b);
-        qkey[qn + rank] = (static_cast<uint32_t>(it) << 18) | (c0 << kCertColBits) |
-                          static_cast<uint32_t>(grp * 256 + 16 * (bit & 15) + r);
-        qscale[qn + rank] = scale;
-        flags &= flags - 1u;
-      }
-      qn += min(__popc(ball), room);
-      if (qn == QN) {
-        cert_drain<DT>(src, K, q_out, qkey, qscale, qn, lane);
-        qn = 0;
+      __syncwarp();
+      if (lane == 0) {  // the buffer is free: reset the record, stage the row after next
+        rc->ncand = 0u;
+        rc->nties = 0u;
+        rc->flags = 0u;
+        const int64_t rn = row + 2 * static_cast<int64_t>(gridDim.x);
+        if (rn < rows) {
+          fence_proxy_async_smem();
+          mbar_arrive_expect_tx(&full[b], row_bytes);
+          bulk_load(buf, src + rn * row_bytes, row_bytes, &full[b]);
+        }
       }
       __syncwarp();
     }
   }
-  if (!failed && qn > 0) cert_drain<DT>(src, K, q_out, qkey, qscale, qn, lane);
-  if (t == 0) {
-    for (int b = 0; b < 2; ++b)
-      if (pending & (1u << b)) mbar_wait(&bar[b], (pending_parity >> b) & 1u, kErrWaitTimeoutDrain);
-  }
 }
 
-// Queue length per warp: 32 (one drain pass of 32 lanes); 16 for rows of 48+ groups, whose
-// 14+ warps must leave room for two CTAs per SM.
-static int cert_queue_len(int threads) { return threads >= 384 ? 16 : 32; }
+// Fixer warps: one for rows of up to 24 groups (the CTA keeps four per SM), two for wider rows.
+static int cert_fixers(int K) { return (K >> 8) > 24 ? 2 : 1; }
 
 size_t cert_smem_bytes(int K, int dtype, int threads) {
   const size_t esz = dtype == kF32 ? 4 : 2;
-  const size_t nw = static_cast<size_t>(threads / 32);
-  return 544 + nw * cert_queue_len(threads) * 8 + 2 * esz * static_cast<size_t>(K) + nw * 2 * 256 * sizeof(float2);
+  const size_t ns = static_cast<size_t>(threads / 32 - cert_fixers(K));
+  return kCertOffRows + 2 * esz * static_cast<size_t>(K) + ns * 2 * 256 * sizeof(float2);
 }
 
-// Rows of 5 <= K/256 <= 64 groups. Inputs with more than 2^18 rows per CTA take the
-// sixteen-output reference kernel instead.
+// Rows of 5 <= K/256 <= 64 groups: the streamer warps (16 threads per group pair) plus the fixers.
 cudaError_t launch_cert_rotate_quant(const void* x, int dtype, int64_t rows, int K, int8_t* q, float* scale,
                                      cudaStream_t st) {
   const int g2 = ((K >> 8) + 1) >> 1;
-  const int threads = (g2 + 1) / 2 * 32;
+  const int nf = cert_fixers(K);
+  const int threads = (g2 + 1) / 2 * 32 + 32 * nf;
   const size_t smem = cert_smem_bytes(K, dtype, threads);
   void (*fn)(const void*, int64_t, int, int8_t*, float*);
-  if (threads >= 384)
-    fn = dtype == kBF16 ? cert_rotate_quant_kernel<kBF16, 72, 16>
-                        : (dtype == kF32 ? cert_rotate_quant_kernel<kF32, 72, 16> : cert_rotate_quant_kernel<kF16, 72, 16>);
+  if (nf == 2)
+    fn = dtype == kBF16 ? cert_rotate_quant_kernel<kBF16, 64, 2>
+                        : (dtype == kF32 ? cert_rotate_quant_kernel<kF32, 64, 2> : cert_rotate_quant_kernel<kF16, 64, 2>);
   else
-    fn = dtype == kBF16 ? cert_rotate_quant_kernel<kBF16, 96, 32>
-                        : (dtype == kF32 ? cert_rotate_quant_kernel<kF32, 96, 32> : cert_rotate_quant_kernel<kF16, 96, 32>);
+    fn = dtype == kBF16 ? cert_rotate_quant_kernel<kBF16, 80, 1>
+                        : (dtype == kF32 ? cert_rotate_quant_kernel<kF32, 80, 1> : cert_rotate_quant_kernel<kF16, 80, 1>);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
@@ -515,7 +613,6 @@ cudaError_t launch_cert_rotate_quant(const void* x, int dtype, int64_t rows, int
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   const int grid = grid_for_rows(rows, per_sm);
-  if ((rows + grid - 1) / grid > kCertMaxIters) return launch_ref_rotate_quant(x, dtype, rows, K, q, scale, st);
   fn<<<grid, threads, smem, st>>>(x, rows, K, q, scale);
   return cudaGetLastError();
 }

@@ -9,7 +9,12 @@
 //           code = E2M1 round-half-even of v, saturating at 6, sign bit kept (0b1000 for
 //                  negative values that round to zero)
 // Every division is IEEE (div.rn); the E4M3 rounding is the hardware cvt.rn.satfinite.
-// Packing: element 2i in the low nibble of byte i (the order the tensor cores read).
+// Packing: element 2i in the HIGH nibble of byte i, element 2i+1 in the low nibble: "two E2M1
+// values per byte, high nibble first", the on-disk layout of slimdit/nvfp4.py:5 and
+// docs/DEV_NOTES.md:64. The codes are formed low nibble first (the order of the hardware
+// conversion) and swapped within each byte on the way out. The FP4 GEMM reads both of its
+// operands in this order: swapping the two elements of every byte in both A and B permutes K
+// identically on both sides, inside each 16-element scale block, so the sums are unchanged.
 // Block scales are written in the cuBLAS 128x4 tiled layout: scale (r, c) of a matrix with
 // C = K/16 scale columns lives at ((r/128)*(C/4) + c/4)*512 + (r%32)*16 + ((r%128)/32)*4 + c%4.
 //
@@ -69,7 +74,12 @@ __device__ __forceinline__ uint32_t e2m1x8(const float2 (&t)[4]) {
   return r;
 }
 
-// One 16-element block -> 8 packed bytes and its scale byte.
+// Exchanges the two nibbles of every byte (low-first <-> high-first packing; an involution).
+__device__ __forceinline__ uint32_t nibble_swap(uint32_t w) {
+  return ((w & 0x0f0f0f0fu) << 4) | ((w >> 4) & 0x0f0f0f0fu);
+}
+
+// One 16-element block -> 8 packed bytes (high nibble first) and its scale byte.
 // The element quotient v = fl(x / total) is not formed. With r = fl(1/total), the products
 // hi = fl(x * fl(r (1 + 2^-19))) and lo = fl(x * fl(r (1 - 2^-19))) bracket v in magnitude
 // (three roundings move each by at most 3 * 2^-24 relative, well inside the 2^-19 offset), and
@@ -119,7 +129,7 @@ __device__ __forceinline__ void quant_block16(const float (&v)[16], float gs, ui
       }
     }
   }
-  packed = make_uint2(w[0], w[1]);
+  packed = make_uint2(nibble_swap(w[0]), nibble_swap(w[1]));
 }
 
 // A thread's 16 input elements as raw 16-byte words (4 for fp32, 2 for 16-bit types): loaded
@@ -393,7 +403,8 @@ __global__ void __launch_bounds__(256) nvfp4_dequant_kernel(const uint8_t* __res
     const int c = static_cast<int>(b - row * nb);
     const float s = __ldg(scale + (per_row ? row : 0));
     const float bs = __fmul_rn(s, e4m3_value(sf[blocked_offset(row, c, ctiles)]));
-    const uint2 pk = *reinterpret_cast<const uint2*>(q + row * (K >> 1) + 8 * c);
+    const uint2 pk_stored = *reinterpret_cast<const uint2*>(q + row * (K >> 1) + 8 * c);
+    const uint2 pk = make_uint2(nibble_swap(pk_stored.x), nibble_swap(pk_stored.y));  // element 2i low
     float v[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {

@@ -67,6 +67,8 @@ cudaError_t launch_quantize_rows(const float* rot, int64_t rows, int K, int8_t* 
 // rows < 2^32, 16-byte aligned input.
 cudaError_t launch_cert_rotate_quant(const void* x, int dtype, int64_t rows, int K, int8_t* q, float* scale,
                                      cudaStream_t st);
+// capi.cu: the linears' activation quantiser (reference order; certified kernel where it applies).
+cudaError_t launch_act_quant(const void* x, int dtype, int64_t rows, int K, int8_t* q, float* scale, cudaStream_t st);
 // Whether launch_cert_rotate_quant takes this shape.
 inline bool cert_supported(int64_t rows, int64_t K) {
   const int64_t g = K / 256;

@@ -499,46 +499,55 @@ def _convert_steps(src_dir, out_path, rank, grid, block_limit, verify_blocks, cu
         else:
             raise ValueError(f"unhandled op kind {op.kind!r}")
 
-    if host_jobs is not None:
-        host_futs = [host_jobs.submit(host_op, op) for op in mine if op.kind != "quant"]
-    errors_by_op: dict[int, float] = {}
-    if piped:
-        piped_errors = _Pipeline(quantizer.device, src, writer, blob, quant_report).run(piped)
-        errors_by_op.update((id(op), e) for op, e in zip(piped, piped_errors))
-    for op in tqdm(mine, unit="op", desc=f"convert[{worker}/{workers}]", disable=workers > 1 and worker != 0):
-        name = op.out[0]
-        if id(op) in piped_ids or (host_jobs is not None and op.kind != "quant"):
-            continue
-        if op.kind == "quant":
-            base = name[: -len(".weight")]
-            parts = [src.get(s) for s in op.src]
-            if quant == "int8_convrot":
-                q, scale, err = quantizer(parts, op.swap_halves, quant_report)
-                writer.write(f"{base}.weight", q.tobytes())
-                writer.write(f"{base}.weight_scale", np.ascontiguousarray(scale, dtype=np.float32).tobytes())
-                writer.write(f"{base}.comfy_quant", blob)
+    # the write phase: on any failure, stop the host jobs and close the file before the failure
+    # reaches the next synchronisation point (where the ranks agree that the conversion failed)
+    try:
+        if host_jobs is not None:
+            host_futs = [host_jobs.submit(host_op, op) for op in mine if op.kind != "quant"]
+        errors_by_op: dict[int, float] = {}
+        if piped:
+            piped_errors = _Pipeline(quantizer.device, src, writer, blob, quant_report).run(piped)
+            errors_by_op.update((id(op), e) for op, e in zip(piped, piped_errors))
+        for op in tqdm(mine, unit="op", desc=f"convert[{worker}/{workers}]", disable=workers > 1 and worker != 0):
+            name = op.out[0]
+            if id(op) in piped_ids or (host_jobs is not None and op.kind != "quant"):
+                continue
+            if op.kind == "quant":
+                base = name[: -len(".weight")]
+                parts = [src.get(s) for s in op.src]
+                if quant == "int8_convrot":
+                    q, scale, err = quantizer(parts, op.swap_halves, quant_report)
+                    writer.write(f"{base}.weight", q.tobytes())
+                    writer.write(f"{base}.weight_scale", np.ascontiguousarray(scale, dtype=np.float32).tobytes())
+                    writer.write(f"{base}.comfy_quant", blob)
+                else:
+                    from . import nvfp4
+                    qd, bs, ts, err = quantizer(parts, op.swap_halves, quant_report)
+                    writer.write(f"{base}.weight", qd.tobytes())
+                    writer.write(f"{base}.weight_scale", bs.tobytes())
+                    writer.write(f"{base}.weight_scale_2", np.float32(ts).tobytes())
+                    writer.write(f"{base}.comfy_quant", nvfp4.comfy_quant_blob().tobytes())
+                if err is not None:
+                    errors_by_op[id(op)] = err
+                del parts
             else:
-                from . import nvfp4
-                qd, bs, ts, err = quantizer(parts, op.swap_halves, quant_report)
-                writer.write(f"{base}.weight", qd.tobytes())
-                writer.write(f"{base}.weight_scale", bs.tobytes())
-                writer.write(f"{base}.weight_scale_2", np.float32(ts).tobytes())
-                writer.write(f"{base}.comfy_quant", nvfp4.comfy_quant_blob().tobytes())
-            if err is not None:
-                errors_by_op[id(op)] = err
-            del parts
-        else:
-            host_op(op)
+                host_op(op)
 
-    for f in host_futs:
-        f.result()
-    if basis_job is not None:
-        table, basis = basis_job.result()
-    if host_jobs is not None:
-        host_jobs.shutdown()
-    report.quant_errors = [errors_by_op[id(op)] for op in mine if id(op) in errors_by_op]
-    expect = {n for op in mine for n in _outputs(op, quant)} | ({"adaln_t_table"} if worker == 0 else set())
-    writer.close(expect=expect)
+        for f in host_futs:
+            f.result()
+        if basis_job is not None:
+            table, basis = basis_job.result()
+        if host_jobs is not None:
+            host_jobs.shutdown()
+        report.quant_errors = [errors_by_op[id(op)] for op in mine if id(op) in errors_by_op]
+        expect = {n for op in mine for n in _outputs(op, quant)} | ({"adaln_t_table"} if worker == 0 else set())
+        writer.close(expect=expect)
+    except BaseException:
+        if host_jobs is not None:
+            host_jobs.shutdown(wait=True, cancel_futures=True)
+        writer.close()
+        src.close()
+        raise
     src.close()
     yield  # synchronisation point 2: every rank's tensors are written
     if workers > 1:

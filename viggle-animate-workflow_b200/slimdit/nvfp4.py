@@ -10,8 +10,8 @@ An NVFP4 linear is stored as (slimdit/nvfp4.py:3-8 of the reference)
 The reference refuses to quantise without ``comfy_kitchen`` (its NVFP4 arithmetic lives
 there). Here the arithmetic runs in libslimdit_b200.so on the GPU: per-tensor amax, block
 scales ``e4m3(min(fl(fl(block_amax / 6) / s2), 448))`` and E2M1 codes rounded half to even
-from ``fl(x / fl(s2 * block_scale))``; element 2i of a row is the low nibble of byte i, the
-order the FP4 tensor cores read. :class:`ComfyKitchenMissing` is kept for API compatibility
+from ``fl(x / fl(s2 * block_scale))``, two per byte with element 2i in the high nibble (the
+documented layout above). :class:`ComfyKitchenMissing` is kept for API compatibility
 and is raised when no sm_100 device or built library is available.
 """
 

@@ -1,9 +1,9 @@
 """Device entry points on torch CUDA tensors (memory comes from torch's allocator; every
 computation runs in libslimdit_b200.so).
 
-* ``rotate_quant``  group-256 Hadamard rotation + per-row INT8 (slimdit/int8.py:39-52 for
-  weights in the reference order; the per-token activation side of the runtime linear in
-  the butterfly order)
+* ``rotate_quant``  group-256 Hadamard rotation + per-row INT8 (slimdit/int8.py:39-52), in the
+  reference's summation order (codes and scales identical to the reference's, for weights
+  and for the per-token activation side of the runtime linear) or the butterfly order
 * ``rotate``        rotation alone, fp32 out (slimdit/hadamard.py:45-58)
 * ``quantize_rows`` quantisation alone (slimdit/int8.py:49-51)
 * ``dequantize``    (q * scale) @ H^T (slimdit/int8.py:55-61)
@@ -149,12 +149,16 @@ def gemm_i8(a: torch.Tensor, b: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor
 
 def int8_linear(x: torch.Tensor, qweight: torch.Tensor, wscales: torch.Tensor, convrot: bool = True,
                 convrot_groupsize: int = 256, out_dtype: torch.dtype = torch.bfloat16,
-                bias: torch.Tensor | None = None, epilogue: str | None = None) -> torch.Tensor:
+                bias: torch.Tensor | None = None, epilogue: str | None = None,
+                order: str = "reference") -> torch.Tensor:
     """Convrot W8A8 linear: y = rot(x) quantised per token @ (qweight * wscales)^T + bias.
 
     x: [..., K] bf16/f16/f32 CUDA; qweight: int8 [N, K] (pre-rotated, slimdit/int8.py:3-11);
     wscales: f32 [N, 1] or [N]. Same call shape as the runtime op the reference uses
     (tools/bench_int8.py:65-68). The output is computed in bf16 and cast if out_dtype differs.
+    order="reference" (slim_int8_linear) quantises the activations exactly as the reference's
+    rotate() + int8.py math would; order="butterfly" uses the fast transform alone
+    (slim_rotate_quant_i8 + slim_gemm_i8).
     """
     nat.require_cuda()
     if not x.is_cuda:
@@ -174,7 +178,12 @@ def int8_linear(x: torch.Tensor, qweight: torch.Tensor, wscales: torch.Tensor, c
     b = _vec(bias, n, torch.bfloat16, dev, "bias")
     n_out = n // 2 if epilogue == "swiglu" else n
     out = torch.empty((m, n_out), dtype=torch.bfloat16, device=dev)
-    if convrot:
+    if order not in _ORDERS:
+        raise ValueError(f"order must be one of {sorted(_ORDERS)}")
+    if convrot and order == "butterfly":
+        xq, sx = rotate_quant(x2, convrot_groupsize, order="butterfly")
+        gemm_i8(xq, qweight, sx, sw, b, epilogue=epilogue, out=out)
+    elif convrot:
         xq = torch.empty((m, k), dtype=torch.int8, device=dev)
         sx = torch.empty((m,), dtype=torch.float32, device=dev)
         with torch.cuda.device(dev):
@@ -191,13 +200,21 @@ def int8_linear(x: torch.Tensor, qweight: torch.Tensor, wscales: torch.Tensor, c
 
 
 def ffn_int8(x: torch.Tensor, w_up: torch.Tensor, s_up: torch.Tensor, w_down: torch.Tensor, s_down: torch.Tensor,
-             b_up: torch.Tensor | None = None, b_down: torch.Tensor | None = None) -> torch.Tensor:
+             b_up: torch.Tensor | None = None, b_down: torch.Tensor | None = None,
+             order: str = "reference") -> torch.Tensor:
     """DiT FFN pair on the convrot linear: down(rotquant(gelu_tanh(up(x)))).
 
     The up-projection's epilogue applies GELU-tanh to its bf16 output (the same rounding as
     running the linear and then the activation on its bf16 result); the hidden activation
-    is rotated and requantised per token before the down-projection.
+    is rotated and requantised per token before the down-projection. order="reference" runs
+    slim_ffn_i8 (reference-order activation codes); order="butterfly" composes the two
+    linears with the fast transform.
     """
+    if order == "butterfly":
+        h = int8_linear(x, w_up, s_up, bias=b_up, epilogue="gelu_tanh", order="butterfly")
+        return int8_linear(h, w_down, s_down, bias=b_down, order="butterfly")
+    if order != "reference":
+        raise ValueError(f"order must be one of {sorted(_ORDERS)}")
     return _ffn(x, w_up, s_up, b_up, w_down, s_down, b_down, "gelu_tanh")
 
 

@@ -146,7 +146,10 @@ class OffsetWriter:
         self.written.add(name)
 
     def close(self, expect: set[str] | None = None) -> None:
-        os.close(self._fd)
+        """Close the file (a second call only repeats the completeness check)."""
+        if self._fd >= 0:
+            os.close(self._fd)
+            self._fd = -1
         if expect is not None and not expect <= self.written:
             missing = sorted(expect - self.written)[:4]
             raise RuntimeError(f"incomplete write: missing {missing}...")
