@@ -5,8 +5,14 @@ Workload (one "step"): the single convrot linear at the QKV shape — X bf16 [32
 (Student-t(4) x 0.5, 16 outlier channels x30), W int8 [15360, 5120] pre-rotated codes with
 fp32 row scales (converted by this library's reference-order converter from N(0, 0.02)
 weights with outlier channels x50), bf16 bias [15360]. One step = per-token rotate +
-quantise of X (butterfly kernel) + tcgen05 INT8 GEMM with the dequant/bias epilogue ->
-bf16 [32768, 15360]. Metric: int8 TOPS (2*M*N*K per step).
+quantise of X in the reference's order (the certified kernel: codes and scales identical to
+the reference's rotate() + int8.py math) + tcgen05 INT8 GEMM with the dequant/bias epilogue
+-> bf16 [32768, 15360]. Metric: int8 TOPS (2*M*N*K per step). The line also counts, on the
+timed input, the codes and scales that the butterfly order alone would change.
+
+Each secondary workload (config-2 FFN pair, real MiniMax-H3 shapes, NVFP4 up-projection,
+converter kernels, attention, converter end to end) prints its own JSON line before the main
+line; the main line (last) carries a compact summary of them.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -14,8 +20,9 @@ N > 1 runs under torchrun, one rank per GPU, each rank its own 32768-token batch
 weights replicated (token rows are independent: no collective on the data path), so the
 scaling is weak; `value` is the aggregate over ranks divided by the slowest rank's time.
 
---impl reference times the CPU restatement of the same linear (oracle: the reference's
-rotation/quantisation math + torch's CPU int8 GEMM) on the host cores, rank 0 only.
+--impl reference times the CPU restatement of the same linear (the reference's rotation,
+np.matmul of the grouped rows with H^T, its per-row quantisation math + torch's CPU int8 GEMM)
+on the host cores, rank 0 only.
 """
 
 from __future__ import annotations
@@ -217,7 +224,8 @@ def cpu_baseline(target_seconds: float) -> dict:
     value = 2.0 * total_rows * N * K / total_t / 1e12
     return {"value": round(value, 4), "unit": "TOPS", "cores": threads, "kind": "port",
             "sample": f"{total_rows} tokens in chunks of {rows} through the 15360x5120 linear "
-                      f"(oracle rotation+quant, torch CPU int8 GEMM), {total_t:.1f} s of CPU time"}
+                      f"(the reference's np.matmul rotation + int8.py quantisation, torch CPU int8 GEMM), "
+                      f"{total_t:.1f} s of CPU time"}
 
 
 def run_reference(args) -> int:
@@ -804,8 +812,9 @@ def run_ours(args) -> int:
     sx = torch.empty((M,), dtype=torch.float32, device=dev)
     out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
 
-    def quant():
-        _native.check(lib.slim_rotate_quant_i8(x.data_ptr(), _native.BF16, M, K, 256, _native.ORDER_BUTTERFLY,
+    def quant(order=_native.ORDER_REFERENCE):
+        # the activation side of slim_int8_linear: reference-order codes (certified kernel)
+        _native.check(lib.slim_rotate_quant_i8(x.data_ptr(), _native.BF16, M, K, 256, order,
                                                xq.data_ptr(), sx.data_ptr(), None, sp))
 
     def gemm():
@@ -819,6 +828,25 @@ def run_ours(args) -> int:
     for _ in range(max(3, args.warmup)):
         quant()
         gemm()
+    torch.cuda.synchronize(dev)
+    # activation parity on this input: the butterfly order against the reference order the step
+    # uses (outside the timed region), and the butterfly quantiser's own time for comparison
+    q_ref, s_ref = xq.clone(), sx.clone()
+    quant(_native.ORDER_BUTTERFLY)
+    torch.cuda.synchronize(dev)
+    parity = {"order_timed": "reference", "rows": M, "K": K,
+              "butterfly_codes_differ": int((xq != q_ref).sum().item()),
+              "butterfly_code_max_abs_diff": int((xq.int() - q_ref.int()).abs().max().item()),
+              "butterfly_scales_differ": int((sx != s_ref).sum().item())}
+    bf_a, bf_b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    bf_a.record(stream)
+    for _ in range(5):
+        quant(_native.ORDER_BUTTERFLY)
+    bf_b.record(stream)
+    torch.cuda.synchronize(dev)
+    parity["butterfly_quant_ms"] = round(bf_a.elapsed_time(bf_b) / 5, 4)
+    del q_ref, s_ref
+    quant()
     torch.cuda.synchronize(dev)
     barrier()
 
@@ -916,6 +944,8 @@ def run_ours(args) -> int:
             peak = 2.0 * (1400.0 if sustained else 1590.0)
             peak_src = f"2 x fallback bf16 {regime}"
         gemm_tops = OPS_PER_STEP / (gemm_ms * 1e-3) / 1e12
+        # DRAM traffic of one GEMM launch is read from the committed summary of an offline ncu
+        # capture of the same shape (a profiler cannot run inside this timed benchmark)
         traffic = None
         prof = ROOT / "profiles" / "gemm_i8_pair_qkv_32768x15360x5120.md"
         if prof.exists():
@@ -934,8 +964,11 @@ def run_ours(args) -> int:
                          "achieved": round(gemm_tops, 2), "peak": round(peak, 1), "unit": "TOPS",
                          "frac": round(gemm_tops / peak, 4), "peak_source": peak_src,
                          "frac_of_nominal_4500": round(gemm_tops / NOMINAL_I8_TOPS, 4), "traffic": traffic,
+                         "traffic_source": "offline ncu capture (dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                           "launch): profiles/gemm_i8_pair_qkv_32768x15360x5120.md",
                          "avg_launch_ms": round(gemm_ms, 4)},
-            "kernels_ms_per_step": {"rotate_quant_butterfly": round(quant_ms, 4), "gemm_i8": round(gemm_ms, 4)},
+            "kernels_ms_per_step": {"rotate_quant_reference_order": round(quant_ms, 4), "gemm_i8": round(gemm_ms, 4)},
+            "activation_parity": parity,
             "act_quant_gbs": round((M * K * 2 + M * K + M * 4) / (quant_ms * 1e-3) / 1e9, 1),
             "gpu_launches": int(launches),
             "clocks": clk,
@@ -951,7 +984,12 @@ def run_ours(args) -> int:
             nv["fp4_peak"] = round(fp4_peak, 1)
             nv["frac_of_fp4_peak"] = round(nv["value"] / (world * fp4_peak), 4)
             nv["gemm_frac_of_fp4_peak"] = round(nv["gemm_value"] / (world * fp4_peak), 4)
-            line["secondary"] = secondary
+            # each secondary workload on its own line (printed below, before this one); this line
+            # keeps a compact summary of their headline figures
+            summary_keys = ("value", "unit", "ms_per_step", "ms_total", "frac_of_i8_peak", "frac_of_fp4_peak",
+                            "gemm_frac_of_fp4_peak", "frac_of_measured_hbm", "tensor_frac_of_int8_peak")
+            line["secondary"] = {name: {k: v[k] for k in summary_keys if k in v} for name, v in secondary.items()
+                                 if isinstance(v, dict)}
         if e2e is not None:
             line["e2e"] = {"value": round(world * OPS_PER_STEP / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TOPS",
                            "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
@@ -960,8 +998,12 @@ def run_ours(args) -> int:
                                   "4096-row chunks overlapped on three streams"}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
-            if "attention_packed" in line.get("secondary", {}):
-                line["secondary"]["attention_packed"]["cpu_baseline"] = attention_cpu_sample(min(args.cpu_seconds, 8.0))
+            if secondary is not None and "attention_packed" in secondary:
+                secondary["attention_packed"]["cpu_baseline"] = attention_cpu_sample(min(args.cpu_seconds, 8.0))
+        if secondary is not None:
+            for name, v in secondary.items():
+                print(json.dumps({"secondary": name, **v} if isinstance(v, dict) else {"secondary": name, "value": v}),
+                      flush=True)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

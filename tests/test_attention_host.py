@@ -66,7 +66,7 @@ def test_config_and_override_rules():
 
     cfg = TritonAttnConfig()
     assert not cfg.enabled and cfg.min_seq == DEFAULT_MIN_SEQ and cfg.rotate
-    assert set(cfg.describe()) == {"block_m", "block_n", "num_warps", "num_stages", "min_seq", "rotate"}
+    assert set(cfg.describe()) == {"kernel", "min_seq", "rotate"}
     with pytest.raises(ValueError):
         TritonAttnOverride(cfg)
 
@@ -94,7 +94,7 @@ def test_install_without_a_gpu(monkeypatch, capsys):
     assert install_triton_attn(TritonAttnConfig(enabled=False)) is None
     # the override still routes calls it cannot take to the original function
     _, (q, k, v) = _views()
-    ov._original = original
+    ov.dense = original
     assert ov(q, k, v, 2, mask=torch.ones(1), skip_reshape=True) == "dense"
 
 

@@ -70,9 +70,10 @@ def test_swapped_gated_projection_is_a_finding(cuda, converted, tmp_path, capsys
     b = q.astype(np.float32) * sc.reshape(-1, 1)
     want = np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b.astype(np.float64))
     dev = torch.device("cuda", 0)
-    d = verify._Dist(dev)
-    got = d.int8(torch.from_numpy(q_sw).to(dev), torch.from_numpy(s_sw).to(dev), torch.from_numpy(q.copy()).to(dev),
-                 torch.from_numpy(sc.copy()).to(dev))
+    d = verify._Distances(dev, 1)
+    d.int8(0, torch.from_numpy(q_sw).to(dev), torch.from_numpy(s_sw).to(dev), torch.from_numpy(q.copy()).to(dev),
+           torch.from_numpy(sc.copy()).to(dev))
+    got = float(d.values()[0])
     assert abs(got - want) <= 1e-9 * want
 
 

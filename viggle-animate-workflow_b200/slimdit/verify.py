@@ -8,10 +8,13 @@ other tensors as stored; a relative L2 error above the tolerance is a finding
 NVFP4 linears against the released bf16 weights and the adaLN curve residual of block 0
 (verify_checkpoint.py:121-152).
 
-The distances are reduced on the device (slim_rel_l2_int8 / slim_rel_l2, fp64 sums); the INT8
-dequantisation for the official mode is the reference-order kernel (bit-identical to
+How it is organised here: a comparison is planned on the host first (which tensors, in which
+form, which ones cannot be compared), then every distance of the plan is reduced on the device
+into one fp64 array (slim_rel_l2_int8 / slim_rel_l2) that is read back once. The INT8
+dequantisation of the official mode is the reference-order kernel (bit-identical to
 slimdit.int8.dequantize_convrot_weight); the curve residual stays on the host with the
-reference's numpy code path.
+reference's numpy code path. Which official tensors make up each quantised linear comes from
+the converter's own key plan (slimdit/mapping.py).
 
     python -m slimdit.verify --checkpoint ours.safetensors --reference reference.safetensors
     python -m slimdit.verify --checkpoint ours.safetensors --official /models/viggle-official
@@ -20,7 +23,7 @@ reference's numpy code path.
 from __future__ import annotations
 
 import argparse
-import re
+import dataclasses
 import sys
 from pathlib import Path
 
@@ -28,19 +31,21 @@ import numpy as np
 import torch
 
 from . import curve as curve_mod
+from . import mapping
 from .int8 import descriptor_fields
 from .safetensors_io import ShardSet
 
-OFFICIAL_FOR = {
-    "attn.qkv_proj.weight": ("attn.to_q.weight", "attn.to_k.weight", "attn.to_v.weight"),
-    "attn.out_proj.weight": ("attn.to_out.0.weight",),
-    "mlp.fc1.weight": ("ff.net.0.proj.weight",),
-    "mlp.fc2.weight": ("ff.net.2.weight",),
-}
+#: quantised linear (suffix inside a block) -> the official tensors it is made of, in order
+OFFICIAL_FOR = {out: srcs for out, srcs, _ in mapping.QUANT_BLOCK_LAYERS}
+#: quantised linears whose two halves the converter exchanges ([gate; up] -> [up; gate])
+SWAPPED = {out for out, _, swap in mapping.QUANT_BLOCK_LAYERS if swap}
 
-#: Curve tensors are derived analytically and differ between releases: excluded from the
-#: reference comparison, covered by the official-weight mode (verify_checkpoint.py:45-47).
-CURVE_KEYS = re.compile(r"adaln_t_table|adaln_proj")
+
+def is_curve_key(key: str) -> bool:
+    """Curve tensors (the shared table and each block's projected adaLN weight) are derived
+    analytically and differ between releases: the reference mode leaves them out, the
+    official mode checks them (verify_checkpoint.py:45-47)."""
+    return key == "adaln_t_table" or ".adaln_proj." in key
 
 
 def _device() -> torch.device:
@@ -50,30 +55,28 @@ def _device() -> torch.device:
     return torch.device("cuda", torch.cuda.current_device())
 
 
-class _Dist:
-    """fp64 [sum (a-b)^2, sum b^2] accumulators on the device."""
+class _Distances:
+    """Relative L2 distances of n tensor pairs, reduced on the device: slot i accumulates
+    [sum (a - b)^2, sum b^2] in fp64; ``values()`` reads all slots back at once."""
 
-    def __init__(self, dev):
+    def __init__(self, dev: torch.device, n: int):
         from . import _native
 
-        self.nat = _native
-        self.lib = _native.load()
-        self.dev = dev
-        self.acc = torch.zeros((2,), dtype=torch.float64, device=dev)
+        self.nat, self.lib, self.dev = _native, _native.load(), dev
+        self.acc = torch.zeros((max(n, 1), 2), dtype=torch.float64, device=dev)
 
-    def rel(self) -> float:
-        e2, b2 = self.acc.cpu().tolist()
-        self.acc.zero_()
-        return float(np.sqrt(e2 / b2)) if b2 else 0.0
+    def _slot(self, i: int) -> int:
+        return self.acc[i].data_ptr()
 
-    def int8(self, qa, sa, qb, sb) -> float:
+    def int8(self, i: int, qa, sa, qb, sb) -> None:
+        """Slot i: INT8 rows in the rotated basis, fl32(q * row scale) on both sides."""
         rows, k = qa.shape
         st = torch.cuda.current_stream(self.dev).cuda_stream
         self.nat.check(self.lib.slim_rel_l2_int8(qa.data_ptr(), sa.data_ptr(), qb.data_ptr(), sb.data_ptr(), rows, k,
-                                                 self.acc.data_ptr(), st))
-        return self.rel()
+                                                 self._slot(i), st))
 
-    def dense(self, a: torch.Tensor, b: torch.Tensor) -> float:
+    def dense(self, i: int, a: torch.Tensor, b: torch.Tensor) -> None:
+        """Slot i: two tensors of float dtypes, compared as fp32 values."""
         from .ops import _DT
 
         a, b = a.contiguous(), b.contiguous()
@@ -82,122 +85,136 @@ class _Dist:
                 raise TypeError(f"cannot compare dtype {t.dtype}")
         st = torch.cuda.current_stream(self.dev).cuda_stream
         self.nat.check(self.lib.slim_rel_l2(a.data_ptr(), _DT[a.dtype], b.data_ptr(), _DT[b.dtype], a.numel(),
-                                            self.acc.data_ptr(), st))
-        return self.rel()
+                                            self._slot(i), st))
+
+    def values(self) -> np.ndarray:
+        e2, b2 = self.acc.cpu().numpy().T
+        with np.errstate(invalid="ignore", divide="ignore"):
+            return np.where(b2 > 0, np.sqrt(e2 / np.where(b2 > 0, b2, 1.0)), 0.0)
 
 
-def _format(src: ShardSet, key: str) -> str | None:
+def _quant_format(src: ShardSet, key: str) -> str | None:
+    """The comfy_quant format of a ``*.weight`` (None for tensors stored as they are)."""
     if not key.endswith(".weight"):
         return None
     desc = key[: -len(".weight")] + ".comfy_quant"
-    if desc not in src.manifest:
-        return None
-    return descriptor_fields(src.get(desc).numpy()).get("format")
+    return descriptor_fields(src.get(desc).numpy()).get("format") if desc in src.manifest else None
 
 
-def _device_value(src: ShardSet, key: str, dev, rotated: bool):
-    """("int8", codes, row scales) in the rotated basis, or ("dense", fp32/bf16/f16 tensor)."""
+def _on_device(src: ShardSet, key: str, dev, rotated: bool):
+    """A tensor in the form it is compared in: ("int8", codes, row scales) in the rotated basis
+    (rotated=True), else ("dense", float tensor) - INT8 linears rotated back to the original
+    basis, NVFP4 linears dequantised, everything else as stored (widened to fp32 if needed)."""
     from . import ops
 
     tensor = src.get(key)
-    fmt = _format(src, key)
-    if fmt == "nvfp4":
-        base = key[: -len(".weight")]
-        q = tensor.to(dev)
-        bs = src.get(f"{base}.weight_scale").view(torch.uint8).to(dev)
-        s2 = src.get(f"{base}.weight_scale_2").float().reshape(1).to(dev)
-        return ("dense", ops.nvfp4_dequantize(q, bs, s2))
-    scale_key = key[: -len(".weight")] + ".weight_scale" if key.endswith(".weight") else None
-    if scale_key is not None and scale_key in src.manifest and tensor.dtype == torch.int8:
-        q = tensor.to(dev)
-        s = src.get(scale_key).float().reshape(-1).to(dev)
-        if rotated:
-            return ("int8", q, s)
-        return ("dense", ops.dequantize(q, s))
+    base = key[: -len(".weight")] if key.endswith(".weight") else None
+    if _quant_format(src, key) == "nvfp4":
+        block_scale = src.get(f"{base}.weight_scale").view(torch.uint8).to(dev)
+        tensor_scale = src.get(f"{base}.weight_scale_2").float().reshape(1).to(dev)
+        return "dense", ops.nvfp4_dequantize(tensor.to(dev), block_scale, tensor_scale)
+    if base is not None and tensor.dtype == torch.int8 and f"{base}.weight_scale" in src.manifest:
+        codes = tensor.to(dev)
+        scales = src.get(f"{base}.weight_scale").float().reshape(-1).to(dev)
+        return ("int8", codes, scales) if rotated else ("dense", ops.dequantize(codes, scales))
     if tensor.dtype not in (torch.float32, torch.bfloat16, torch.float16):
         tensor = tensor.float()
-    return ("dense", tensor.to(dev))
+    return "dense", tensor.to(dev)
+
+
+@dataclasses.dataclass
+class _Plan:
+    """What a reference comparison does, decided before any device work."""
+
+    compared: list[str]          # every shared, non-curve key
+    one_sided: list[str]         # keys present in only one of the two checkpoints
+    descriptors: list[str]       # comfy_quant tensors: compared byte for byte
+    distances: list[str]         # tensors whose distance is measured on the device
+    format_skipped: int          # stored in a different quantisation format on the two sides
+
+
+def _plan(ours: ShardSet, ref: ShardSet) -> _Plan:
+    shared = sorted(k for k in ours.manifest.keys() & ref.manifest.keys() if not is_curve_key(k))
+    descriptors = [k for k in shared if k.endswith(".comfy_quant")]
+    rest = [k for k in shared if not k.endswith(".comfy_quant")]
+    same_format = [k for k in rest if _quant_format(ours, k) == _quant_format(ref, k)]
+    return _Plan(compared=shared, one_sided=sorted(ours.manifest.keys() ^ ref.manifest.keys()),
+                 descriptors=descriptors, distances=same_format, format_skipped=len(rest) - len(same_format))
 
 
 def compare_reference(ours: ShardSet, ref: ShardSet, tolerance: float, limit: int) -> int:
+    """The reference mode: prints the report, returns the number of findings."""
     dev = _device()
-    dist = _Dist(dev)
-    shared = sorted(k for k in set(ours.manifest) & set(ref.manifest) if not CURVE_KEYS.search(k))
-    mismatched_layout = sorted(set(ours.manifest) ^ set(ref.manifest))
-    worst: list[tuple[float, str]] = []
-    failures = 0
-    skipped_format = 0
-    for key in shared:
-        if key.endswith(".comfy_quant"):
-            if bytes(ours.get(key).numpy().tobytes()) != bytes(ref.get(key).numpy().tobytes()):
-                print(f"  DESCRIPTOR MISMATCH {key}")
-                failures += 1
+    plan = _plan(ours, ref)
+    findings = 0
+    for key in plan.descriptors:
+        if ours.get(key).numpy().tobytes() != ref.get(key).numpy().tobytes():
+            print(f"  DESCRIPTOR MISMATCH {key}")
+            findings += 1
+    dist = _Distances(dev, len(plan.distances))
+    measured: list[str] = []
+    for key in plan.distances:
+        a, b = _on_device(ours, key, dev, rotated=True), _on_device(ref, key, dev, rotated=True)
+        if a[0] != b[0] or a[1].shape != b[1].shape:
+            print(f"  SHAPE MISMATCH {key}: {tuple(a[1].shape)} vs {tuple(b[1].shape)}")
+            findings += 1
             continue
-        if _format(ours, key) != _format(ref, key):
-            skipped_format += 1
-            continue
-        a, b = _device_value(ours, key, dev, rotated=True), _device_value(ref, key, dev, rotated=True)
-        shape_a = tuple(a[1].shape)
-        shape_b = tuple(b[1].shape)
-        if shape_a != shape_b or a[0] != b[0]:
-            print(f"  SHAPE MISMATCH {key}: {shape_a} vs {shape_b}")
-            failures += 1
-            continue
-        rel = dist.int8(a[1], a[2], b[1], b[2]) if a[0] == "int8" else dist.dense(a[1], b[1])
-        worst.append((rel, key))
-    worst.sort(reverse=True)
-    print(f"compared {len(shared)} tensors (curve keys excluded); {len(mismatched_layout)} keys unique to one side")
-    if skipped_format:
-        print(f"  {skipped_format} tensors skipped: different quantization format than the reference")
-    if mismatched_layout:
-        print(f"  one-sided keys (first 5): {mismatched_layout[:5]}")
+        slot = len(measured)
+        if a[0] == "int8":
+            dist.int8(slot, a[1], a[2], b[1], b[2])
+        else:
+            dist.dense(slot, a[1], b[1])
+        measured.append(key)
+    rel = dist.values()[: len(measured)]
+    order = np.argsort(-rel, kind="stable")
+    print(f"compared {len(plan.compared)} tensors (curve keys excluded); {len(plan.one_sided)} keys unique to one side")
+    if plan.format_skipped:
+        print(f"  {plan.format_skipped} tensors skipped: different quantization format than the reference")
+    if plan.one_sided:
+        print(f"  one-sided keys (first 5): {plan.one_sided[:5]}")
     print(f"worst {limit} deviations from the reference:")
-    for rel, key in worst[:limit]:
-        flag = "FAIL" if rel > tolerance else "ok  "
-        print(f"  [{flag}] {rel * 100:9.4f}%  {key}")
-    failures += sum(1 for rel, _ in worst if rel > tolerance)
-    print(f">>> {failures} findings (tolerance {tolerance * 100:.2f}%)")
-    return failures
+    for i in order[:limit]:
+        print(f"  [{'FAIL' if rel[i] > tolerance else 'ok  '}] {rel[i] * 100:9.4f}%  {measured[i]}")
+    findings += int((rel > tolerance).sum())
+    print(f">>> {findings} findings (tolerance {tolerance * 100:.2f}%)")
+    return findings
+
+
+def _official_weight(official: ShardSet, key: str, dev) -> torch.Tensor:
+    """The released bf16 weight that quantised linear ``key`` (blocks.<i>.<suffix>) was made
+    from, assembled the way the converter assembles it (slimdit/mapping.py)."""
+    _, block, suffix = key.split(".", 2)
+    parts = [official.get(f"transformer_blocks.{block}.{name}").to(dev) for name in OFFICIAL_FOR[suffix]]
+    weight = torch.cat(parts, dim=0) if len(parts) > 1 else parts[0]
+    if suffix in SWAPPED:  # the runtime's swiglu takes [up; gate]; the release stores [gate; up]
+        weight = torch.cat(weight.chunk(2, dim=0)[::-1], dim=0)
+    return weight
 
 
 def official_quant_errors(slim: ShardSet, official: ShardSet, layers: list[str]) -> dict[str, float]:
     """Relative conversion error of each named linear against the official bf16 weights."""
     dev = _device()
-    dist = _Dist(dev)
-    out = {}
-    for key in layers:
-        block = key.split(".")[1]
-        suffix = key.split(".", 2)[2]
-        parts = [official.get(f"transformer_blocks.{block}.{n}").to(dev) for n in OFFICIAL_FOR[suffix]]
-        ref = parts[0] if len(parts) == 1 else torch.cat(parts, dim=0)
-        if suffix == "mlp.fc1.weight":
-            # the runtime's swiglu takes [up; gate]; the released checkpoint stores [gate; up]
-            half = ref.shape[0] // 2
-            ref = torch.cat([ref[half:], ref[:half]], dim=0)
-        restored = _device_value(slim, key, dev, rotated=False)[1]
-        out[key] = dist.dense(restored, ref)
-    return out
+    dist = _Distances(dev, len(layers))
+    for slot, key in enumerate(layers):
+        dist.dense(slot, _on_device(slim, key, dev, rotated=False)[1], _official_weight(official, key, dev))
+    return dict(zip(layers, (float(v) for v in dist.values())))
 
 
 def compare_official(slim: ShardSet, official: ShardSet, layers: list[str], rank: int, grid: int) -> int:
-    failures = 0
-    for key, rel in official_quant_errors(slim, official, layers).items():
+    """The official-weight mode: prints the report, returns the number of findings."""
+    errors = official_quant_errors(slim, official, layers)
+    for key, rel in errors.items():
         print(f"  {key}: quant error {rel * 100:.4f}%")
-        failures += rel > 0.15
-    emb = (
-        official.get("time_embedder.linear_1.weight").float().numpy(),
-        official.get("time_embedder.linear_1.bias").float().numpy(),
-        official.get("time_embedder.linear_2.weight").float().numpy(),
-        official.get("time_embedder.linear_2.bias").float().numpy(),
-    )
-    table = slim.get("adaln_t_table").float().numpy()
-    curve = curve_mod.silu(curve_mod.time_embeddings(np.linspace(0, 1, grid, dtype=np.float32), *emb))
-    weight = official.get("transformer_blocks.0.adaln_proj.linear.weight").float().numpy()
-    projected = slim.get("blocks.0.adaln_proj.linear.weight").float().numpy()
-    residual = curve_mod.curve_residual(weight, curve, table, projected)
+    findings = sum(rel > 0.15 for rel in errors.values())
+    embedder = [official.get(f"time_embedder.{name}").float().numpy()
+                for name in ("linear_1.weight", "linear_1.bias", "linear_2.weight", "linear_2.bias")]
+    t = np.linspace(0, 1, grid, dtype=np.float32)
+    curve = curve_mod.silu(curve_mod.time_embeddings(t, *embedder))
+    residual = curve_mod.curve_residual(official.get("transformer_blocks.0.adaln_proj.linear.weight").float().numpy(),
+                                        curve, slim.get("adaln_t_table").float().numpy(),
+                                        slim.get("blocks.0.adaln_proj.linear.weight").float().numpy())
     print(f"  blocks.0 curve: modulation error {residual * 100:.5f}% (rank {rank}, grid {grid})")
-    failures += residual > 5e-4
-    return failures
+    return findings + int(residual > 5e-4)
 
 
 def main(argv: list[str] | None = None) -> int:
@@ -211,16 +228,17 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--grid", type=int, default=1025)
     args = ap.parse_args(argv)
 
-    slim = ShardSet(Path(args.checkpoint))
-    print(f"checkpoint: {args.checkpoint} ({len(slim.manifest)} tensors)")
-    failures = 0
+    checkpoint = ShardSet(Path(args.checkpoint))
+    print(f"checkpoint: {args.checkpoint} ({len(checkpoint.manifest)} tensors)")
+    modes = []
     if args.reference:
-        failures += compare_reference(slim, ShardSet(Path(args.reference)), args.tolerance, 10)
+        modes.append(lambda: compare_reference(checkpoint, ShardSet(Path(args.reference)), args.tolerance, 10))
     if args.official:
-        failures += compare_official(slim, ShardSet(args.official), [k.strip() for k in args.layers.split(",") if k.strip()],
-                                     args.rank, args.grid)
-    print("CONTENTS OK" if not failures else f"CONTENTS SUSPECT ({failures} findings)")
-    return 0 if not failures else 1
+        layers = [name.strip() for name in args.layers.split(",") if name.strip()]
+        modes.append(lambda: compare_official(checkpoint, ShardSet(args.official), layers, args.rank, args.grid))
+    findings = sum(mode() for mode in modes)
+    print("CONTENTS OK" if not findings else f"CONTENTS SUSPECT ({findings} findings)")
+    return 1 if findings else 0
 
 
 if __name__ == "__main__":
