@@ -62,7 +62,7 @@ def parse_args(argv=None):
     ap.add_argument("--no-secondary", action="store_true", help="skip the FFN and converter measurements")
     ap.add_argument("--secondary-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU work in the cpu_baseline sample")
-    ap.add_argument("--profile-case", choices=["nvfp4", "attn", "rotate"], default=None,
+    ap.add_argument("--profile-case", choices=["nvfp4", "attn", "rotate", "actquant", "hidquant"], default=None,
                     help="run only a small case of one workload (for ncu captures; prints no bench line)")
     ap.add_argument("--tokens", type=int, default=16384, help="token rows of the --profile-case run")
     ap.add_argument("--heads", type=int, default=4, help="attention heads of the --profile-case attn run")
@@ -688,6 +688,43 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
 
 
 # ----------------------------------------------------------------------------- profiling cases
+def run_profile_quant(args, hidden: bool) -> int:
+    """The linears' activation quantiser (reference order, certified kernel) alone on `--tokens`
+    rows: config-1 activations (K 5120), or with `hidden` the config-2 FFN hidden (K 13824, GELU-
+    tanh of twice the config-1 distribution). Warm-up + `--steps` calls, for ncu captures."""
+    import torch
+
+    from slimdit import _native, ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    k = 13824 if hidden else K
+    g = torch.Generator(device=dev)
+    g.manual_seed(12)
+    z = torch.randn((args.tokens, k), generator=g, device=dev)
+    chi2 = torch._standard_gamma(torch.full((args.tokens, k), 2.0, device=dev), generator=g) * 2.0
+    x = z / torch.sqrt(chi2 / 4.0) * 0.5
+    del z, chi2
+    x[:, torch.randperm(k, generator=g, device=dev)[:16]] *= 30.0
+    if hidden:
+        x = torch.nn.functional.gelu(2.0 * x, approximate="tanh")
+    x = x.to(torch.bfloat16)
+    warm = max(1, args.warmup)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    for i in range(warm + args.steps):
+        if i == warm:
+            ev[0].record()
+        ops.rotate_quant(x, order="reference")
+    ev[1].record()
+    torch.cuda.synchronize(dev)
+    assert _native.device_error() == 0
+    ms = ev[0].elapsed_time(ev[1]) / max(1, args.steps)
+    print(json.dumps({"profile_case": "hidden_quant" if hidden else "activation_quant", "rows": args.tokens, "K": k,
+                      "steps": args.steps, "ms": round(ms, 4),
+                      "GBs": round(args.tokens * (3 * k + 4) / (ms * 1e-3) / 1e9, 1)}))
+    return 0
+
+
 def run_profile_rotate(args) -> int:
     """The reference-order weight rotation + INT8 of one linear (W bf16 [tokens, 5120], the QKV
     linear's 15360 rows by default in captures): warm-up + `--steps` calls, for ncu captures."""
@@ -1017,6 +1054,8 @@ def main(argv=None) -> int:
         return run_reference(args)
     if args.profile_case == "rotate":
         return run_profile_rotate(args)
+    if args.profile_case in ("actquant", "hidquant"):
+        return run_profile_quant(args, hidden=args.profile_case == "hidquant")
     if args.profile_case == "attn":
         return run_profile_attn(args)
     if args.profile_case:

@@ -317,3 +317,64 @@ def test_first_calls_from_many_threads_at_once(cuda):
     paths = [str(root / "viggle-animate-workflow_b200"), str(root), str(root / "tests")]
     r = subprocess.run([sys.executable, "-c", _THREADS_SCRIPT, *paths], capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "threads ok" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
+
+
+def test_ffn_config2_slice_stage_by_stage(cuda):
+    """The config-2 FFN on 2048 tokens (5120 -> 13824 -> 5120, GELU-tanh), through the C entry
+    slim_ffn_i8 with the test's own workspaces, checked stage by stage:
+    * activation codes/scales = the reference-order quantisation of x (bit-exact);
+    * hidden bf16 h: within 2 bf16 ulp of GELU-tanh (fp64) of the oracle's bf16 up-projection (one
+      ulp from the epilogue's own rounding, one where the pre-activation sits on a bf16 rounding
+      boundary); at most 1 in 10^4 beyond 1 ulp;
+    * hidden codes/scales = the reference-order quantisation of the GPU's own h (bit-exact), and
+      against the codes of the oracle's fp32 GELU: the approximate exponential in the epilogue
+      changes at most 1 in 10^4 codes, each by one;
+    * output within 1 bf16 ulp of the fp64 dequant of the GPU's own hidden codes."""
+    from slimdit import _native
+    from slimdit.int8 import quantize_convrot_weight
+    m, k, f = 2048, 5120, 13824
+    x = synthetic.activations(m, k, seed=21)
+    qu, su = quantize_convrot_weight(synthetic.weight(f, k, seed=22))
+    qd, sd = quantize_convrot_weight(synthetic.weight(k, f, seed=23))
+    dev = cuda
+    xt = torch.from_numpy(x).to(dev).to(torch.bfloat16)
+    t = {name: torch.from_numpy(a).to(dev) for name, a in (("qu", qu), ("su", su.reshape(-1)), ("qd", qd),
+                                                           ("sd", sd.reshape(-1)))}
+    xq = torch.empty((m, k), dtype=torch.int8, device=dev)
+    sx = torch.empty((m,), dtype=torch.float32, device=dev)
+    h = torch.empty((m, f), dtype=torch.bfloat16, device=dev)
+    hq = torch.empty((m, f), dtype=torch.int8, device=dev)
+    sh = torch.empty((m,), dtype=torch.float32, device=dev)
+    out = torch.empty((m, k), dtype=torch.bfloat16, device=dev)
+    lib = _native.load()
+    _native.check(lib.slim_ffn_i8(xt.data_ptr(), _native.BF16, t["qu"].data_ptr(), t["su"].data_ptr(), None,
+                                  t["qd"].data_ptr(), t["sd"].data_ptr(), None, out.data_ptr(), xq.data_ptr(),
+                                  sx.data_ptr(), h.data_ptr(), hq.data_ptr(), sh.data_ptr(), m, k, f,
+                                  _native.EPI_GELU_TANH, None))
+    torch.cuda.synchronize()
+    # stage 1: activation codes
+    qx, sxo = oracle.quantize_activations(x)
+    assert np.array_equal(xq.cpu().numpy(), qx)
+    assert np.array_equal(sx.cpu().numpy().view(np.uint32), sxo.reshape(-1).view(np.uint32))
+    # stage 2: the hidden activation
+    acc1 = oracle.int8_gemm_i32(qx, qu)
+    lin = oracle.bf16_round((acc1.astype(np.float64) * sxo.reshape(-1, 1) * su.reshape(1, -1)).astype(np.float32))
+    l64 = lin.astype(np.float64)
+    gelu64 = 0.5 * l64 * (1.0 + np.tanh(0.7978845608028654 * (l64 + 0.044715 * l64 ** 3)))
+    hv = h.cpu().float().numpy().astype(np.float64)
+    ulp = oracle.bf16_ulp(gelu64) + 2.0**-133
+    assert np.all(np.abs(hv - gelu64) <= 2 * ulp), float((np.abs(hv - gelu64) / ulp).max())
+    assert (np.abs(hv - gelu64) > ulp).mean() <= 1e-4
+    # stage 3: hidden codes of the GPU's own h, and against the oracle's fp32 GELU
+    h_gpu = h.cpu().float().numpy()
+    qh, sho = oracle.quantize_activations(h_gpu)
+    hq_n = hq.cpu().numpy()
+    assert np.array_equal(hq_n, qh)
+    assert np.array_equal(sh.cpu().numpy().view(np.uint32), sho.reshape(-1).view(np.uint32))
+    qh_o, _ = oracle.quantize_activations(oracle.bf16_round(oracle.gelu_tanh_f32(lin)))
+    diff = hq_n.astype(np.int32) - qh_o.astype(np.int32)
+    assert np.abs(diff).max() <= 1
+    assert (diff != 0).mean() <= 1e-4, int((diff != 0).sum())
+    # stage 4: the output against the GPU's own hidden codes
+    acc2 = oracle.int8_gemm_i32(hq_n, qd)
+    check_bf16_within_one_ulp(out, oracle.linear_reference_f64(acc2, sho.reshape(-1), sd.reshape(-1), None), "ffn out")
