@@ -360,7 +360,8 @@ def test_ffn_config2_slice_stage_by_stage(cuda):
     acc1 = oracle.int8_gemm_i32(qx, qu)
     lin = oracle.bf16_round((acc1.astype(np.float64) * sxo.reshape(-1, 1) * su.reshape(1, -1)).astype(np.float32))
     l64 = lin.astype(np.float64)
-    gelu64 = 0.5 * l64 * (1.0 + np.tanh(0.7978845608028654 * (l64 + 0.044715 * l64 ** 3)))
+    # GELU-tanh as x / (1 + exp(-2u)) (= 0.5 x (1 + tanh u) exactly): no cancellation where tanh -> -1
+    gelu64 = l64 / (1.0 + np.exp(-2.0 * 0.7978845608028654 * (l64 + 0.044715 * l64 ** 3)))
     hv = h.cpu().float().numpy().astype(np.float64)
     ulp = oracle.bf16_ulp(gelu64) + 2.0**-133
     assert np.all(np.abs(hv - gelu64) <= 2 * ulp), float((np.abs(hv - gelu64) / ulp).max())

@@ -141,7 +141,7 @@ __device__ __forceinline__ float cert_chunk_steps(float acc, const uint4* q, con
 
 // The reference chain for output j of one group (grp = its 256 inputs in shared memory, c0 as in
 // step 1): S_ref = fl-chain of sum_k sign(j, k) x_k over k = 0..255, sign(j, k) = sig(b) lam(l)
-// for k = 16 b + l. Chunks below c0 are summed exactly, two at a time (any grouping is exact
+// for k = 16 b + l. Chunks below c0 are summed exactly, four at a time (any grouping is exact
 // there). From chunk c0 on the accumulator is carried as sig(b) * acc, so every step is
 // fma(x, lam_l, acc) with an exact product and a chunk change multiplies it by sig(b) sig(b-1)
 // = +-1 (rounding to nearest is symmetric, so the carried chain rounds exactly like the plain
@@ -160,13 +160,17 @@ __device__ __forceinline__ float cert_chain(const unsigned char* grp, int j, int
   constexpr int kChunk = 16 * CertFmt<DT>::kEsz;
   float pa = 0.0f, pb = 0.0f;
   int b = 0;
-  for (; b + 2 <= c0; b += 2) {
-    const float ta = cert_chunk_steps<DT>(0.0f, reinterpret_cast<const uint4*>(grp + b * kChunk), lp, lam);
-    const float tb = cert_chunk_steps<DT>(0.0f, reinterpret_cast<const uint4*>(grp + (b + 1) * kChunk), lp, lam);
-    pa = __fmaf_rn(ta, h4sign(j3, b >> 2) * h4sign(j2, b & 3), pa);
-    pb = __fmaf_rn(tb, h4sign(j3, (b + 1) >> 2) * h4sign(j2, (b + 1) & 3), pb);
+  for (; b + 4 <= c0; b += 4) {  // chunks b..b+3 share digit 3 of b; their digit 2 is 0..3
+    const uint4* q = reinterpret_cast<const uint4*>(grp + b * kChunk);
+    const float t0 = cert_chunk_steps<DT>(0.0f, q, lp, lam);
+    const float t1 = cert_chunk_steps<DT>(0.0f, q + kChunk / 16, lp, lam);
+    const float t2 = cert_chunk_steps<DT>(0.0f, q + 2 * (kChunk / 16), lp, lam);
+    const float t3 = cert_chunk_steps<DT>(0.0f, q + 3 * (kChunk / 16), lp, lam);
+    const float s3 = h4sign(j3, b >> 2);
+    pa = __fmaf_rn(__fmaf_rn(t0, h4sign(j2, 0), t2 * h4sign(j2, 2)), s3, pa);
+    pb = __fmaf_rn(__fmaf_rn(t1, h4sign(j2, 1), t3 * h4sign(j2, 3)), s3, pb);
   }
-  if (b < c0) {
+  for (; b < c0; ++b) {
     const float ta = cert_chunk_steps<DT>(0.0f, reinterpret_cast<const uint4*>(grp + b * kChunk), lp, lam);
     pa = __fmaf_rn(ta, h4sign(j3, b >> 2) * h4sign(j2, b & 3), pa);
   }
@@ -534,9 +538,7 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
   } else {
     // ------------------------------------------------------------ fixers
     // Fixer f takes the rows of iterations f, f + NF, ... (with two fixers, fixer f owns buffer
-    // f). Per row, two phases over listed columns, one output per lane, one chain code path:
-    //   phase 0: the maximum (uncertain rows: the candidates; overflowed rows: every output),
-    //   phase 1: the codes (the listed near-tie outputs; overflowed rows: every output).
+    // f); one output per lane.
     for (int it = warp - ns; blockIdx.x + static_cast<int64_t>(it) * gridDim.x < rows; it += NF) {
       const int b = it & 1;
       const int64_t row = blockIdx.x + static_cast<int64_t>(it) * gridDim.x;
@@ -549,17 +551,48 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
       const int64_t rbase = row * static_cast<int64_t>(K);
       float scale = rc->scale;
       float m = rc->a0;
-      for (int phase = (all || (flags & kCertUnsure)) ? 0 : 1; phase < 2; ++phase) {
-        const int n = all ? K : static_cast<int>(phase == 0 ? rc->ncand : rc->nties);
-        const uint16_t* list = phase == 0 ? cands + b * kCertCand : ties + b * kCertTies;
-        for (int e = lane; e < n; e += 32) {
-          const int col = all ? e : list[e];
-          const float S = cert_chain<DT>(buf + (col & ~255) * kEsz, col & 255, c0tab[col >> 8]);
-          if (phase == 0) m = fmaxf(m, fabsf(S));
-          else q_out[rbase + col] = quant_code(__fmul_rn(S, 0.0625f), scale);
+      if (flags & kCertOverflow) {
+        // every output by its chain: the maximum first (phase 0), then the codes (phase 1)
+        for (int phase = 0; phase < 2; ++phase) {
+          for (int col = lane; col < K; col += 32) {
+            const float S = cert_chain<DT>(buf + (col & ~255) * kEsz, col & 255, c0tab[col >> 8]);
+            if (phase == 0) m = fmaxf(m, fabsf(S));
+            else q_out[rbase + col] = quant_code(__fmul_rn(S, 0.0625f), scale);
+          }
+          if (phase == 0) {
+            m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
+            scale = cert_scale(m);
+            if (lane == 0) scale_out[row] = scale;
+          }
         }
-        if (phase == 0) {
-          m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
+      } else {
+        // one pass per 32 listed outputs, the candidates first: a chain's value does not depend
+        // on the scale, so a near-tie output in the pass that completes the candidates takes its
+        // code as soon as their maximum settles the scale
+        const bool unsure = (flags & kCertUnsure) != 0u;
+        const int nc = unsure ? static_cast<int>(rc->ncand) : 0;
+        const int n = nc + static_cast<int>(rc->nties);
+        bool settled = !unsure;
+        for (int base = 0; base < n; base += 32) {
+          const int e = base + lane;
+          int col = 0;
+          float S = 0.0f;
+          if (e < n) {
+            col = e < nc ? cands[b * kCertCand + e] : ties[b * kCertTies + (e - nc)];
+            S = cert_chain<DT>(buf + (col & ~255) * kEsz, col & 255, c0tab[col >> 8]);
+          }
+          if (!settled) {
+            if (e < nc) m = fmaxf(m, fabsf(S));
+            if (base + 32 >= nc) {  // every candidate is done (the same for all lanes)
+              m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
+              scale = cert_scale(m);
+              if (lane == 0) scale_out[row] = scale;
+              settled = true;
+            }
+          }
+          if (e >= nc && e < n) q_out[rbase + col] = quant_code(__fmul_rn(S, 0.0625f), scale);
+        }
+        if (!settled) {  // an uncertain row with nothing listed: the exact part is the maximum
           scale = cert_scale(m);
           if (lane == 0) scale_out[row] = scale;
         }
