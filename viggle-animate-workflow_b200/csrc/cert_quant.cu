@@ -265,6 +265,15 @@ __device__ __forceinline__ uint32_t cert_codes(const float2 (&v)[16], float rm, 
   return near;
 }
 
+// Float exchange buffer of one half-warp (16 rows x 16 floats): the 16-byte slot of a row is
+// XOR-permuted by the row, and the second half-warp of a warp (h = 1) takes row rho ^ 1 for row
+// rho, so the row-wise 16-byte writes and the column-wise 4-byte reads of the whole warp are
+// free of bank conflicts (the two half-warps read complementary 16-bank halves).
+__device__ __forceinline__ int xposf(int row, int col, int h) {
+  const int pr = row ^ h;
+  return 16 * pr + 4 * ((col >> 2) ^ ((pr >> 1) & 3)) + (col & 3);
+}
+
 // ------------------------------------------------------------------ the kernel
 // Per staged row: a record and two lists (columns of the outputs whose chain is needed), filled by
 // the streamer warps and settled by the fixer warp that owns the row's buffer.
@@ -278,13 +287,25 @@ struct CertRec {
 };
 constexpr uint32_t kCertUnsure = 1u, kCertOverflow = 2u;
 constexpr int kCertCand = 64;   // candidate list length per row
-constexpr int kCertTies = 512;  // near-tie list length per row
+constexpr int kCertTies = 448;  // near-tie list length per row
 
-// Shared-memory layout (bytes): mbarriers full[2] (row staged), done[2] (streamers finished a
-// row), cbar (streamer block barrier); failure flag; warp partials; records; per-group c0; lists;
-// then the two staged rows and the streamers' transpose buffers.
-constexpr int kCertOffFull = 0, kCertOffDone = 16, kCertOffCbar = 32, kCertOffFail = 40, kCertOffRed = 48;
-constexpr int kCertOffRec = 432, kCertOffC0 = 496, kCertOffCand = 624, kCertOffTies = 880, kCertOffRows = 2944;
+// Shared-memory layout (bytes) for NB staging buffers: mbarriers full[NB] (row staged), done[NB]
+// (streamers finished a row), cbar (streamer block barrier); failure flag; warp partials (two
+// row parities); per buffer a record, the per-group c0 and the two lists; then the NB staged rows
+// and the streamers' transpose buffers.
+template <int NB>
+struct CertLayout {
+  static constexpr int kFull = 0;
+  static constexpr int kDone = 8 * NB;
+  static constexpr int kCbar = 16 * NB;
+  static constexpr int kFail = kCbar + 8;
+  static constexpr int kRed = kFail + 8;                                   // [2][3 kinds][16 warps] floats
+  static constexpr int kRec = kRed + 2 * 3 * 16 * 4;                       // [NB] CertRec
+  static constexpr int kC0 = kRec + NB * static_cast<int>(sizeof(CertRec));  // [NB][64]
+  static constexpr int kCand = kC0 + NB * 64;                              // [NB][kCertCand] uint16
+  static constexpr int kTies = kCand + NB * kCertCand * 2;                 // [NB][kCertTies] uint16
+  static constexpr int kRows = (kTies + NB * kCertTies * 2 + 127) & ~127;
+};
 
 // Appends this lane's outputs (mask bits: bit i < 16 -> group p, else group p + G2; output
 // 16 (i & 15) + r) to a row list with one atomic per warp; on overflow flags the record instead.
@@ -333,9 +354,10 @@ __device__ __forceinline__ float cert_scale(float absmax_s) { return row_scale_f
 // interval that contains it), provisional codes, and list the outputs whose chain is needed.
 // NF fixer warps (the last ones) follow the streamers: a fixer runs the listed chains of a row
 // from its staging buffer in shared memory (one output per lane), settles the row's scale and
-// codes, and then reuses the buffer for the row after next. Rows arrive by bulk copies, two
-// buffers; with two fixers each owns one buffer.
-template <int DT, int MAXR, int NF>
+// codes, and then restages the buffer with the row NB iterations on. Rows arrive by bulk copies
+// into NB buffers (iteration i uses buffer i % NB), so the streamers run up to NB - 1 rows ahead
+// of the fixers: a fixer's chains plus the restaging copy hide behind NB - 1 streamer rows.
+template <int DT, int MAXR, int NF, int NB, bool XH>
 __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restrict__ x, int64_t rows, int K,
                                                            int8_t* __restrict__ q_out,
                                                            float* __restrict__ scale_out) {
@@ -345,29 +367,30 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
   const int t = threadIdx.x;
   const int warp = t >> 5, lane = t & 31;
   const int ns = (blockDim.x >> 5) - NF;  // streamer warps; the last NF warps are the fixers
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kCertOffFull);
-  uint64_t* done = reinterpret_cast<uint64_t*>(smem_raw + kCertOffDone);
-  uint64_t* cbar = reinterpret_cast<uint64_t*>(smem_raw + kCertOffCbar);
-  volatile uint32_t* fail_flag = reinterpret_cast<volatile uint32_t*>(smem_raw + kCertOffFail);
-  float* red = reinterpret_cast<float*>(smem_raw + kCertOffRed);  // [2 parities][3 kinds][16 warps]
-  CertRec* recs = reinterpret_cast<CertRec*>(smem_raw + kCertOffRec);
-  uint8_t* c0tabs = smem_raw + kCertOffC0;                           // [2][64]
-  uint16_t* cands = reinterpret_cast<uint16_t*>(smem_raw + kCertOffCand);  // [2][kCertCand]
-  uint16_t* ties = reinterpret_cast<uint16_t*>(smem_raw + kCertOffTies);   // [2][kCertTies]
-  unsigned char* rowbuf = smem_raw + kCertOffRows;                   // 2 staged rows
-  float2* xbuf = reinterpret_cast<float2*>(rowbuf + 2 * static_cast<size_t>(row_bytes));
+  using L = CertLayout<NB>;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + L::kFull);
+  uint64_t* done = reinterpret_cast<uint64_t*>(smem_raw + L::kDone);
+  uint64_t* cbar = reinterpret_cast<uint64_t*>(smem_raw + L::kCbar);
+  volatile uint32_t* fail_flag = reinterpret_cast<volatile uint32_t*>(smem_raw + L::kFail);
+  float* red = reinterpret_cast<float*>(smem_raw + L::kRed);  // [2 parities][3 kinds][16 warps]
+  CertRec* recs = reinterpret_cast<CertRec*>(smem_raw + L::kRec);
+  uint8_t* c0tabs = smem_raw + L::kC0;                           // [NB][64]
+  uint16_t* cands = reinterpret_cast<uint16_t*>(smem_raw + L::kCand);  // [NB][kCertCand]
+  uint16_t* ties = reinterpret_cast<uint16_t*>(smem_raw + L::kTies);   // [NB][kCertTies]
+  unsigned char* rowbuf = smem_raw + L::kRows;                   // NB staged rows
+  float2* xbuf = reinterpret_cast<float2*>(rowbuf + NB * static_cast<size_t>(row_bytes));
   const unsigned char* src = static_cast<const unsigned char*>(x);
   const int G = K >> 8;
   const int G2 = (G + 1) >> 1;
 
   if (t == 0) {
-    mbar_init(&full[0], 1);
-    mbar_init(&full[1], 1);
-    mbar_init(&done[0], static_cast<uint32_t>(ns));
-    mbar_init(&done[1], static_cast<uint32_t>(ns));
+    for (int b = 0; b < NB; ++b) {
+      mbar_init(&full[b], 1);
+      mbar_init(&done[b], static_cast<uint32_t>(ns));
+    }
     mbar_init(cbar, static_cast<uint32_t>(ns));
     *fail_flag = 0u;
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NB; ++b) {
       recs[b].ncand = 0u;
       recs[b].nties = 0u;
       recs[b].flags = 0u;
@@ -376,7 +399,7 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
   }
   __syncthreads();
   if (t == 0) {
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NB; ++b) {
       const int64_t rb = blockIdx.x + b * static_cast<int64_t>(gridDim.x);
       if (rb < rows) {
         mbar_arrive_expect_tx(&full[b], row_bytes);
@@ -391,12 +414,18 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
     const int r = t & 15;  // chunk within the group
     const bool act_a = p < G2;
     const bool act_b = p + G2 < G;
-    float2* gbuf = xbuf + (warp * 2 + ((lane >> 4) & 1)) * 256;
+    const int h = (lane >> 4) & 1;
+    // transpose buffer: XH = the x and y lanes in turn through 256 floats per half-warp, else
+    // both at once through 256 float2
+    float2* gbuf = XH ? reinterpret_cast<float2*>(reinterpret_cast<float*>(xbuf) + (warp * 2 + h) * 256)
+                      : xbuf + (warp * 2 + h) * 256;
+    float* hb = reinterpret_cast<float*>(gbuf);
     uint32_t cparity = 0;
     int64_t row = blockIdx.x;
     for (int it = 0; row < rows; row += gridDim.x, ++it) {
-      const int b = it & 1;
-      if (!mbar_wait(&full[b], (it >> 1) & 1, kErrWaitTimeoutProducer)) *fail_flag = 1u;
+      const int b = it % NB;
+      const int par = it & 1;  // slot of the warp partials
+      if (!mbar_wait(&full[b], (it / NB) & 1, kErrWaitTimeoutProducer)) *fail_flag = 1u;
       CertRec* rc = recs + b;
       const unsigned char* stage = rowbuf + b * row_bytes;
       const int ea = p * 256 + 16 * r;  // element offset of chunk a in the row
@@ -421,9 +450,15 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
           v[i] = make_float2(fa[i], fb[i]);
         }
         bfly16x2(v);  // digits 0, 1
+        if (XH) {
 #pragma unroll
-        for (int i = 0; i < 16; i += 2)
-          *reinterpret_cast<float4*>(gbuf + xpos2(r, i)) = make_float4(v[i].x, v[i].y, v[i + 1].x, v[i + 1].y);
+          for (int i = 0; i < 16; i += 4)
+            *reinterpret_cast<float4*>(hb + xposf(r, i, h)) = make_float4(v[i].x, v[i + 1].x, v[i + 2].x, v[i + 3].x);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; i += 2)
+            *reinterpret_cast<float4*>(gbuf + xpos2(r, i)) = make_float4(v[i].x, v[i].y, v[i + 1].x, v[i + 1].y);
+        }
       }
       int c0a, c0b;
       float Da = cert_group_bound<DT>(l1a, mna, r, lane, c0a);
@@ -436,9 +471,28 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
       }
       __syncwarp();
       float ama = 0.0f, amb = 0.0f;
-      if (act_a) {
+      if (XH) {  // the y lanes after the x lanes (warp-wide syncs outside the per-pair branch)
+        if (act_a) {
 #pragma unroll
-        for (int rr = 0; rr < 16; ++rr) v[rr] = gbuf[xpos2(rr, r)];
+          for (int rr = 0; rr < 16; ++rr) v[rr].x = hb[xposf(rr, r, h)];
+        }
+        __syncwarp();
+        if (act_a) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4)
+            *reinterpret_cast<float4*>(hb + xposf(r, i, h)) = make_float4(v[i].y, v[i + 1].y, v[i + 2].y, v[i + 3].y);
+        }
+        __syncwarp();
+        if (act_a) {
+#pragma unroll
+          for (int rr = 0; rr < 16; ++rr) v[rr].y = hb[xposf(rr, r, h)];
+        }
+      }
+      if (act_a) {
+        if (!XH) {
+#pragma unroll
+          for (int rr = 0; rr < 16; ++rr) v[rr] = gbuf[xpos2(rr, r)];
+        }
         bfly16x2(v);  // digits 2, 3: lanes hold S' for outputs 16 rr + r of groups p and p + G2
 #pragma unroll
         for (int rr = 0; rr < 16; ++rr) {
@@ -454,15 +508,15 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
         const unsigned w1 = __reduce_max_sync(0xffffffffu, __float_as_uint(tA));
         const unsigned w2 = __reduce_max_sync(0xffffffffu, __float_as_uint(tB));
         if (lane == 0) {
-          red[(b * 3 + 0) * 16 + warp] = __uint_as_float(w0);
-          red[(b * 3 + 1) * 16 + warp] = __uint_as_float(w1);
-          red[(b * 3 + 2) * 16 + warp] = __uint_as_float(w2);
+          red[(par * 3 + 0) * 16 + warp] = __uint_as_float(w0);
+          red[(par * 3 + 1) * 16 + warp] = __uint_as_float(w1);
+          red[(par * 3 + 2) * 16 + warp] = __uint_as_float(w2);
         }
       }
       if (!cert_streamer_sync(cbar, cparity, lane) || *fail_flag != 0u) break;  // error recorded
-      const float A0 = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < ns ? __float_as_uint(red[(b * 3 + 0) * 16 + lane]) : 0u));
-      const float A = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < ns ? __float_as_uint(red[(b * 3 + 1) * 16 + lane]) : 0u));
-      const float B = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < ns ? __float_as_uint(red[(b * 3 + 2) * 16 + lane]) : 0u));
+      const float A0 = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < ns ? __float_as_uint(red[(par * 3 + 0) * 16 + lane]) : 0u));
+      const float A = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < ns ? __float_as_uint(red[(par * 3 + 1) * 16 + lane]) : 0u));
+      const float B = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < ns ? __float_as_uint(red[(par * 3 + 2) * 16 + lane]) : 0u));
       // the scale, or (maximum uncertain) an interval [s_lo, s_hi] that contains it; codes are
       // taken from S' rm, and an output's code is certain unless S' rm lies within
       // 2^-13 + D r_hi + |S'| w of a half-integer (w covers the interval; 0 for a certain scale)
@@ -537,17 +591,15 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
     }
   } else {
     // ------------------------------------------------------------ fixers
-    // Fixer f takes the rows of iterations f, f + NF, ... (with two fixers, fixer f owns buffer
-    // f); one output per lane.
+    // Fixer f takes the rows of iterations f, f + NF, ...; one output per lane.
     for (int it = warp - ns; blockIdx.x + static_cast<int64_t>(it) * gridDim.x < rows; it += NF) {
-      const int b = it & 1;
+      const int b = it % NB;
       const int64_t row = blockIdx.x + static_cast<int64_t>(it) * gridDim.x;
-      if (!mbar_wait(&done[b], (it >> 1) & 1, kErrWaitTimeoutDrain)) break;  // streamers stopped
+      if (!mbar_wait(&done[b], (it / NB) & 1, kErrWaitTimeoutDrain)) break;  // streamers stopped
       CertRec* rc = recs + b;
       unsigned char* buf = rowbuf + b * row_bytes;
       const uint8_t* c0tab = c0tabs + b * 64;
       const uint32_t flags = rc->flags;
-      const bool all = (flags & kCertOverflow) != 0u;
       const int64_t rbase = row * static_cast<int64_t>(K);
       float scale = rc->scale;
       float m = rc->a0;
@@ -598,11 +650,11 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
         }
       }
       __syncwarp();
-      if (lane == 0) {  // the buffer is free: reset the record, stage the row after next
+      if (lane == 0) {  // the buffer is free: reset the record, stage the row NB iterations on
         rc->ncand = 0u;
         rc->nties = 0u;
         rc->flags = 0u;
-        const int64_t rn = row + 2 * static_cast<int64_t>(gridDim.x);
+        const int64_t rn = row + NB * static_cast<int64_t>(gridDim.x);
         if (rn < rows) {
           fence_proxy_async_smem();
           mbar_arrive_expect_tx(&full[b], row_bytes);
@@ -614,13 +666,44 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
   }
 }
 
-// Fixer warps: one for rows of up to 24 groups (the CTA keeps four per SM), two for wider rows.
-static int cert_fixers(int K) { return (K >> 8) > 24 ? 2 : 1; }
+// Configuration by row width. Rows of up to 24 groups: one fixer warp, 80 registers, full
+// float2 transposes (four CTAs per SM at K = 5120). Wider rows: two fixer warps, 64 registers and
+// the half-size transpose buffer, which is what lets three staged rows of K = 13824 keep two CTAs
+// per SM. Three staged rows where they fit in a CTA's shared memory without fewer CTAs per SM
+// than two would give, else two: measured on B200 (bit-identical outputs), 32768 x 5120 bf16
+// activations 0.269 -> 0.266 ms and the FFN hidden 115200 x 13824 2.91 -> 2.73 ms with three;
+// four rows, or the half transpose on narrow rows (+11 % time), were slower.
+static bool cert_wide(int K) { return (K >> 8) > 24; }
+static int cert_fixers(int K) { return cert_wide(K) ? 2 : 1; }
+constexpr size_t kCertSmemPerSM = 233472, kCertSmemPerBlock = 232448, kCertSmemReserved = 1024;  // sm_100
 
-size_t cert_smem_bytes(int K, int dtype, int threads) {
+static size_t cert_smem_bytes_nb(int K, int dtype, int threads, int nb) {
   const size_t esz = dtype == kF32 ? 4 : 2;
   const size_t ns = static_cast<size_t>(threads / 32 - cert_fixers(K));
-  return kCertOffRows + 2 * esz * static_cast<size_t>(K) + ns * 2 * 256 * sizeof(float2);
+  const size_t head = nb == 3 ? CertLayout<3>::kRows : CertLayout<2>::kRows;
+  return head + nb * esz * static_cast<size_t>(K) + ns * (cert_wide(K) ? 2048 : 4096);
+}
+
+static int cert_buffers(int K, int dtype, int threads) {
+  const size_t s3 = cert_smem_bytes_nb(K, dtype, threads, 3), s2 = cert_smem_bytes_nb(K, dtype, threads, 2);
+  if (s3 > kCertSmemPerBlock) return 2;
+  const size_t cap = std::min(static_cast<size_t>(65536 / (threads * (cert_wide(K) ? 64 : 80))),
+                              static_cast<size_t>(2048 / threads));
+  const size_t per3 = std::min(cap, kCertSmemPerSM / (s3 + kCertSmemReserved));
+  const size_t per2 = std::min(cap, kCertSmemPerSM / (s2 + kCertSmemReserved));
+  return per3 >= per2 ? 3 : 2;
+}
+
+size_t cert_smem_bytes(int K, int dtype, int threads) {
+  return cert_smem_bytes_nb(K, dtype, threads, cert_buffers(K, dtype, threads));
+}
+
+template <bool kWide, int NB>
+static void (*cert_kernel_for(int dtype))(const void*, int64_t, int, int8_t*, float*) {
+  constexpr int kMaxR = kWide ? 64 : 80, kNF = kWide ? 2 : 1;
+  return dtype == kBF16 ? cert_rotate_quant_kernel<kBF16, kMaxR, kNF, NB, kWide>
+                        : (dtype == kF32 ? cert_rotate_quant_kernel<kF32, kMaxR, kNF, NB, kWide>
+                                         : cert_rotate_quant_kernel<kF16, kMaxR, kNF, NB, kWide>);
 }
 
 // Rows of 5 <= K/256 <= 64 groups: the streamer warps (16 threads per group pair) plus the fixers.
@@ -629,14 +712,11 @@ cudaError_t launch_cert_rotate_quant(const void* x, int dtype, int64_t rows, int
   const int g2 = ((K >> 8) + 1) >> 1;
   const int nf = cert_fixers(K);
   const int threads = (g2 + 1) / 2 * 32 + 32 * nf;
-  const size_t smem = cert_smem_bytes(K, dtype, threads);
-  void (*fn)(const void*, int64_t, int, int8_t*, float*);
-  if (nf == 2)
-    fn = dtype == kBF16 ? cert_rotate_quant_kernel<kBF16, 64, 2>
-                        : (dtype == kF32 ? cert_rotate_quant_kernel<kF32, 64, 2> : cert_rotate_quant_kernel<kF16, 64, 2>);
-  else
-    fn = dtype == kBF16 ? cert_rotate_quant_kernel<kBF16, 80, 1>
-                        : (dtype == kF32 ? cert_rotate_quant_kernel<kF32, 80, 1> : cert_rotate_quant_kernel<kF16, 80, 1>);
+  const int nb = cert_buffers(K, dtype, threads);
+  const size_t smem = cert_smem_bytes_nb(K, dtype, threads, nb);
+  void (*fn)(const void*, int64_t, int, int8_t*, float*) =
+      cert_wide(K) ? (nb == 3 ? cert_kernel_for<true, 3>(dtype) : cert_kernel_for<true, 2>(dtype))
+                   : (nb == 3 ? cert_kernel_for<false, 3>(dtype) : cert_kernel_for<false, 2>(dtype));
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
