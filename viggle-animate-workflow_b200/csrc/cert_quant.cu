@@ -278,8 +278,8 @@ __device__ __forceinline__ int xposf(int row, int col, int h) {
 // Per staged row: a record and two lists (columns of the outputs whose chain is needed), filled by
 // the streamer warps and settled by the fixer warp that owns the row's buffer.
 struct CertRec {
-  uint32_t ncand;     // candidates for the row maximum (uncertain rows only)
-  uint32_t nties;     // outputs whose code waits for its chain
+  uint32_t counts;    // list lengths: candidates for the row maximum (bits 16-31), near ties (0-15)
+  uint32_t pad0;
   uint32_t flags;     // kCertUnsure: the scale is settled by the fixer; kCertOverflow: a list overflowed
   float a0;           // exact part of the row maximum (S units)
   float scale;        // the row scale (certain rows)
@@ -307,31 +307,40 @@ struct CertLayout {
   static constexpr int kRows = (kTies + NB * kCertTies * 2 + 127) & ~127;
 };
 
-// Appends this lane's outputs (mask bits: bit i < 16 -> group p, else group p + G2; output
-// 16 (i & 15) + r) to a row list with one atomic per warp; on overflow flags the record instead.
-__device__ __forceinline__ void cert_append(uint32_t mask, int p, int G2, int r, int lane, uint16_t* list,
-                                            uint32_t* count, uint32_t cap, uint32_t* flags) {
-  if (!__any_sync(0xffffffffu, mask != 0u)) return;
-  const int n = __popc(mask);
-  int incl = n;
-#pragma unroll
-  for (int d = 1; d < 32; d <<= 1) {
-    const int u = __shfl_up_sync(0xffffffffu, incl, d);
-    if (lane >= d) incl += u;
-  }
-  const int total = __shfl_sync(0xffffffffu, incl, 31);
+// Appends this lane's candidates and near ties (mask bits: bit i < 16 -> group p, else group
+// p + G2; output 16 (i & 15) + r) to the row's two lists: one warp reduction and one atomic on
+// the packed counter reserve the warp's entries in both lists (neither half can carry: a row
+// has at most 16384 outputs), then one ballot round per set bit places each lane's entries.
+// On overflow the record is flagged instead.
+__device__ __forceinline__ void cert_append(uint32_t cand, uint32_t near, int p, int G2, int r, int lane,
+                                            uint16_t* clist, uint16_t* tlist, uint32_t* counts, uint32_t* flags) {
+  const uint32_t mine = (static_cast<uint32_t>(__popc(cand)) << 16) | static_cast<uint32_t>(__popc(near));
+  const uint32_t total = __reduce_add_sync(0xffffffffu, mine);
+  if (total == 0u) return;
   uint32_t base = 0;
-  if (lane == 0) base = atomicAdd(count, static_cast<uint32_t>(total));
+  if (lane == 0) base = atomicAdd(counts, total);
   base = __shfl_sync(0xffffffffu, base, 0);
-  if (base + static_cast<uint32_t>(total) > cap) {
+  uint32_t kc = base >> 16, kt = base & 0xffffu;
+  if (kc + (total >> 16) > static_cast<uint32_t>(kCertCand) || kt + (total & 0xffffu) > static_cast<uint32_t>(kCertTies)) {
     if (lane == 0) atomicOr(flags, kCertOverflow);
     return;
   }
-  uint32_t k = base + static_cast<uint32_t>(incl - n);
-  while (mask != 0u) {
-    const int bit = __ffs(mask) - 1;
-    mask &= mask - 1u;
-    list[k++] = static_cast<uint16_t>((bit < 16 ? p : p + G2) * 256 + 16 * (bit & 15) + r);
+  const uint32_t lt = (1u << lane) - 1u;
+  while (__any_sync(0xffffffffu, (cand | near) != 0u)) {
+    const bool hc = cand != 0u, ht = near != 0u;
+    const uint32_t bc = __ballot_sync(0xffffffffu, hc), bt = __ballot_sync(0xffffffffu, ht);
+    if (hc) {
+      const int bit = __ffs(cand) - 1;
+      cand &= cand - 1u;
+      clist[kc + __popc(bc & lt)] = static_cast<uint16_t>((bit < 16 ? p : p + G2) * 256 + 16 * (bit & 15) + r);
+    }
+    if (ht) {
+      const int bit = __ffs(near) - 1;
+      near &= near - 1u;
+      tlist[kt + __popc(bt & lt)] = static_cast<uint16_t>((bit < 16 ? p : p + G2) * 256 + 16 * (bit & 15) + r);
+    }
+    kc += __popc(bc);
+    kt += __popc(bt);
   }
 }
 
@@ -391,8 +400,7 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
     mbar_init(cbar, static_cast<uint32_t>(ns));
     *fail_flag = 0u;
     for (int b = 0; b < NB; ++b) {
-      recs[b].ncand = 0u;
-      recs[b].nties = 0u;
+      recs[b].counts = 0u;
       recs[b].flags = 0u;
     }
     fence_mbar_init();
@@ -545,11 +553,17 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
         near = unsure ? cert_codes<true>(v, rm, w, lim_a, lim_b, cbuf, r) : cert_codes<false>(v, rm, w, lim_a, lim_b, cbuf, r);
         if (tiny_row) near = ~0u;
         if (!act_b) near &= 0xffffu;
+        // a thread's outputs of a group can hold the maximum only if its largest |S'| + D reaches
+        // A (upward rounding is monotone), so most threads skip the per-output test
+        const bool ca = Da > 0.0f && __fadd_ru(ama, Da) >= A;
+        const bool cb = Db > 0.0f && __fadd_ru(amb, Db) >= A;
         if (unsure) {
+          if (ca || cb) {
 #pragma unroll
-          for (int rr = 0; rr < 16; ++rr) {
-            if (Da > 0.0f && __fadd_ru(fabsf(v[rr].x), Da) >= A) cand |= 1u << rr;
-            if (Db > 0.0f && __fadd_ru(fabsf(v[rr].y), Db) >= A) cand |= 1u << (16 + rr);
+            for (int rr = 0; rr < 16; ++rr) {
+              if (ca && __fadd_ru(fabsf(v[rr].x), Da) >= A) cand |= 1u << rr;
+              if (cb && __fadd_ru(fabsf(v[rr].y), Db) >= A) cand |= 1u << (16 + rr);
+            }
           }
         } else {
           // exact groups with a certain scale: S' = S_ref, the IEEE division settles the code here
@@ -582,8 +596,7 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
         *reinterpret_cast<uint4*>(q_out + rbase + ea) = oa;
         if (act_b) *reinterpret_cast<uint4*>(q_out + rbase + eb) = ob;
       }
-      cert_append(cand, p, G2, r, lane, cands + b * kCertCand, &rc->ncand, kCertCand, &rc->flags);
-      cert_append(near, p, G2, r, lane, ties + b * kCertTies, &rc->nties, kCertTies, &rc->flags);
+      cert_append(cand, near, p, G2, r, lane, cands + b * kCertCand, ties + b * kCertTies, &rc->counts, &rc->flags);
       // provisional codes and lists complete before the fixer takes the row
       __threadfence_block();
       __syncwarp();
@@ -622,8 +635,9 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
         // on the scale, so a near-tie output in the pass that completes the candidates takes its
         // code as soon as their maximum settles the scale
         const bool unsure = (flags & kCertUnsure) != 0u;
-        const int nc = unsure ? static_cast<int>(rc->ncand) : 0;
-        const int n = nc + static_cast<int>(rc->nties);
+        const uint32_t cnt = rc->counts;
+        const int nc = unsure ? static_cast<int>(cnt >> 16) : 0;
+        const int n = nc + static_cast<int>(cnt & 0xffffu);
         bool settled = !unsure;
         for (int base = 0; base < n; base += 32) {
           const int e = base + lane;
@@ -651,8 +665,7 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
       }
       __syncwarp();
       if (lane == 0) {  // the buffer is free: reset the record, stage the row NB iterations on
-        rc->ncand = 0u;
-        rc->nties = 0u;
+        rc->counts = 0u;
         rc->flags = 0u;
         const int64_t rn = row + NB * static_cast<int64_t>(gridDim.x);
         if (rn < rows) {
