@@ -58,10 +58,16 @@ __device__ __forceinline__ uint32_t e2m1_code(float v) {
   return c | ((__float_as_uint(v) >> 28) & 8u);
 }
 
-// Eight values -> eight E2M1 codes in one word, value 2i in the low nibble of byte i: the
-// hardware conversion rounds to the nearest grid point and saturates at 6 (ties never reach
-// it here, see quant_block16); the sign is the value's.
-__device__ __forceinline__ uint32_t e2m1x8(const float2 (&t)[4]) {
+// Exchanges the two nibbles of every byte (low-first <-> high-first packing; an involution).
+__device__ __forceinline__ uint32_t nibble_swap(uint32_t w) {
+  return ((w & 0x0f0f0f0fu) << 4) | ((w >> 4) & 0x0f0f0f0fu);
+}
+
+// Eight values -> eight E2M1 codes in one word, value i in nibble i (value 2i in the low nibble
+// of byte i): the hardware conversion rounds to the nearest grid point and saturates at 6 (ties
+// never reach it, see below); the sign is the value's.
+__device__ __forceinline__ uint32_t e2m1x8(float a0, float a1, float a2, float a3, float a4, float a5, float a6,
+                                           float a7) {
   uint32_t r;
   asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
       "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
@@ -70,16 +76,12 @@ __device__ __forceinline__ uint32_t e2m1x8(const float2 (&t)[4]) {
       "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
       "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
       : "=r"(r)
-      : "f"(t[0].x), "f"(t[0].y), "f"(t[1].x), "f"(t[1].y), "f"(t[2].x), "f"(t[2].y), "f"(t[3].x), "f"(t[3].y));
+      : "f"(a0), "f"(a1), "f"(a2), "f"(a3), "f"(a4), "f"(a5), "f"(a6), "f"(a7));
   return r;
 }
 
-// Exchanges the two nibbles of every byte (low-first <-> high-first packing; an involution).
-__device__ __forceinline__ uint32_t nibble_swap(uint32_t w) {
-  return ((w & 0x0f0f0f0fu) << 4) | ((w >> 4) & 0x0f0f0f0fu);
-}
-
-// One 16-element block -> 8 packed bytes (high nibble first) and its scale byte.
+// One 16-element block -> 8 packed bytes (high nibble first) and its scale byte: quant_block16
+// for one block; block_scale + block_codes2 for two blocks in the lanes of packed registers.
 // The element quotient v = fl(x / total) is not formed. With r = fl(1/total), the products
 // hi = fl(x * fl(r (1 + 2^-19))) and lo = fl(x * fl(r (1 - 2^-19))) bracket v in magnitude
 // (three roundings move each by at most 3 * 2^-24 relative, well inside the 2^-19 offset), and
@@ -88,6 +90,76 @@ __device__ __forceinline__ uint32_t nibble_swap(uint32_t w) {
 // exact tie: about 1e-5 of the elements) the IEEE division decides; so does every element of a
 // block whose reciprocal is not finite. The sign is x's (a zero quotient keeps x's sign, as
 // the division's).
+
+// Scale byte, element divisor and bracketing reciprocals of one block from its absmax bm; bad =
+// every code of the block must come from the IEEE division.
+struct BlockScale {
+  uint32_t sfb;
+  float total, rh, rl;
+  bool bad;
+};
+
+__device__ __forceinline__ BlockScale block_scale(float bm, float gs) {
+  BlockScale s;
+  s.sfb = 0;
+  if (gs > 0.0f) s.sfb = e4m3_rne(fminf(__fdiv_rn(__fdiv_rn(bm, 6.0f), gs), 448.0f));
+  s.total = __fmul_rn(gs, e4m3_value(s.sfb));
+  const float rcp = s.total != 0.0f ? __frcp_rn(s.total) : 0.0f;
+  s.bad = !(rcp <= 3.402823466e38f);
+  s.rh = __fmul_rn(rcp, 1.0f + 1.9073486328125e-6f);
+  s.rl = __fmul_rn(rcp, 1.0f - 1.9073486328125e-6f);
+  return s;
+}
+
+// Replaces the codes of the flagged elements (bits of d) of one block with the IEEE division's.
+__device__ __forceinline__ void block_fixup(const float2 (&v)[16], bool lane_y, float total, uint32_t (&w)[2],
+                                            const uint32_t (&d)[2]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t sh = 4 * (i & 7);
+    if ((d[i >> 3] >> sh) & 15u) {
+      const uint32_t code = e2m1_code(__fdiv_rn(lane_y ? v[i].y : v[i].x, total));
+      w[i >> 3] = (w[i >> 3] & ~(15u << sh)) | (code << sh);
+    }
+  }
+}
+
+// Codes of a thread's two blocks (lane x: block a, lane y: block b) from the bracketing
+// products, eight element pairs at a time; the IEEE division where they disagree; 0 where the
+// divisor is 0. Packed high nibble first.
+__device__ __forceinline__ void block_codes2(const float2 (&v)[16], const BlockScale& sa, const BlockScale& sb,
+                                             uint2& pa, uint2& pb) {
+  const float2 rh = make_float2(sa.rh, sb.rh), rl = make_float2(sa.rl, sb.rl);
+  uint32_t wa[2], wb[2], da[2], db[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    float2 th[8], tl[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      th[j] = mul2(v[8 * h + j], rh);
+      tl[j] = mul2(v[8 * h + j], rl);
+    }
+    wa[h] = e2m1x8(th[0].x, th[1].x, th[2].x, th[3].x, th[4].x, th[5].x, th[6].x, th[7].x);
+    da[h] = wa[h] ^ e2m1x8(tl[0].x, tl[1].x, tl[2].x, tl[3].x, tl[4].x, tl[5].x, tl[6].x, tl[7].x);
+    wb[h] = e2m1x8(th[0].y, th[1].y, th[2].y, th[3].y, th[4].y, th[5].y, th[6].y, th[7].y);
+    db[h] = wb[h] ^ e2m1x8(tl[0].y, tl[1].y, tl[2].y, tl[3].y, tl[4].y, tl[5].y, tl[6].y, tl[7].y);
+  }
+  if (sa.bad) da[0] = da[1] = 0xffffffffu;
+  if (sb.bad) db[0] = db[1] = 0xffffffffu;
+  if (sa.total == 0.0f) {
+    wa[0] = wa[1] = 0u;
+  } else if ((da[0] | da[1]) != 0u) {
+    block_fixup(v, false, sa.total, wa, da);
+  }
+  if (sb.total == 0.0f) {
+    wb[0] = wb[1] = 0u;
+  } else if ((db[0] | db[1]) != 0u) {
+    block_fixup(v, true, sb.total, wb, db);
+  }
+  pa = make_uint2(nibble_swap(wa[0]), nibble_swap(wa[1]));
+  pb = make_uint2(nibble_swap(wb[0]), nibble_swap(wb[1]));
+}
+
 __device__ __forceinline__ void quant_block16(const float (&v)[16], float gs, uint2& packed, uint32_t& sfb) {
   float bm = 0.0f;
 #pragma unroll
@@ -114,8 +186,8 @@ __device__ __forceinline__ void quant_block16(const float (&v)[16], float gs, ui
           th[j] = mul2(x2, make_float2(rh, rh));
           tl[j] = mul2(x2, make_float2(rl, rl));
         }
-        w[h] = e2m1x8(th);
-        d[h] = w[h] ^ e2m1x8(tl);
+        w[h] = e2m1x8(th[0].x, th[0].y, th[1].x, th[1].y, th[2].x, th[2].y, th[3].x, th[3].y);
+        d[h] = w[h] ^ e2m1x8(tl[0].x, tl[0].y, tl[1].x, tl[1].y, tl[2].x, tl[2].y, tl[3].x, tl[3].y);
       }
     }
     if ((d[0] | d[1]) != 0u) {
@@ -176,6 +248,17 @@ __device__ __forceinline__ void load16(const void* x, int64_t e0, float (&f)[16]
   unpack16<DT>(load_raw16<DT>(x, e0), f);
 }
 
+constexpr int kQuantMaxStages = 3;
+
+template <int DT>
+__device__ __forceinline__ Raw16<DT> smem_raw16(const unsigned char* stage, int t) {
+  Raw16<DT> r;
+  const uint4* p = reinterpret_cast<const uint4*>(stage) + t * (DT == kF32 ? 4 : 2);
+#pragma unroll
+  for (int e = 0; e < (DT == kF32 ? 4 : 2); ++e) r.w[e] = p[e];
+  return r;
+}
+
 // Radix-4 butterfly step b_i = ((a0 + a1) + (a2 + a3)) - 2*a_{3-i}, each operation rounded
 // to fp32 (the product 2*a is exact, so the fma rounds once, like the subtraction).
 __device__ __forceinline__ void bfly4(float& a0, float& a1, float& a2, float& a3) {
@@ -206,17 +289,6 @@ __device__ __forceinline__ int xpos(int row, int col) {
 // registers. Rows in [rows, rows_pad)
 // only get zero scale bytes (padding of the last 128-row tile).
 // ROW_SCALE: global scale per row (written to row_scale); else per tensor from *amax_in.
-constexpr int kQuantMaxStages = 3;
-
-template <int DT>
-__device__ __forceinline__ Raw16<DT> smem_raw16(const unsigned char* stage, int t) {
-  Raw16<DT> r;
-  const uint4* p = reinterpret_cast<const uint4*>(stage) + t * (DT == kF32 ? 4 : 2);
-#pragma unroll
-  for (int e = 0; e < (DT == kF32 ? 4 : 2); ++e) r.w[e] = p[e];
-  return r;
-}
-
 template <int DT, bool ROT, bool ROW_SCALE>
 __global__ void __launch_bounds__(1024) nvfp4_quant_kernel(const void* __restrict__ x, int64_t rows,
                                                            int64_t rows_pad, int K,
@@ -343,6 +415,167 @@ __global__ void __launch_bounds__(1024) nvfp4_quant_kernel(const void* __restric
   }
 }
 
+// One CTA per row (persistent over rows). Blocks (16 elements, one scale byte) are taken in
+// pairs: with G = ceil(K/256) groups of 16 blocks and G2 = ceil(G/2), thread t (t < 16 G2)
+// owns block t in lane x and block t + 16 G2 in lane y of packed fp32x2 registers, i.e. thread
+// (p, r) holds chunk r of groups p and p + G2, the layout of the INT8 path's group-pair
+// butterfly, whose packed arithmetic gives bit-identical rotated values. Rows are staged in
+// shared memory by bulk copies, nst (1..3, as many as shared memory holds) rows ahead: the HBM
+// reads of the next rows overlap this row's arithmetic without holding registers. Rows in
+// [rows, rows_pad) only get zero scale bytes (padding of the last 128-row tile).
+// ROW_SCALE as in nvfp4_quant_kernel. Rotated rows of up to 8192 elements take this kernel: measured
+// against nvfp4_quant_kernel (bit-identical outputs), 115200 x 5120 rotated bf16 0.696 -> 0.577 ms;
+// at K = 13824 (one CTA of 14 warps per SM at 95 registers) and without the rotation the
+// one-block-per-thread kernel is faster (0.296 vs 0.310 ms; 0.151 vs 0.170 ms).
+template <int DT, bool ROT, bool ROW_SCALE>
+__global__ void __launch_bounds__(512) nvfp4_quant_pair_kernel(const void* __restrict__ x, int64_t rows,
+                                                           int64_t rows_pad, int K,
+                                                           const float* __restrict__ amax_in,
+                                                           uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
+                                                           float* __restrict__ row_scale, int nst) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ float red[2][32];
+  const int NST = nst;
+  constexpr int kEsz = DT == kF32 ? 4 : 2;
+  const uint32_t row_bytes = static_cast<uint32_t>(K) * kEsz;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);                   // up to 3 mbarriers
+  unsigned char* stages = smem_raw + 32;                                   // NST staged rows
+  float2* xch = reinterpret_cast<float2*>(stages + NST * static_cast<size_t>(row_bytes));
+  const unsigned char* src = static_cast<const unsigned char*>(x);
+  const int t = threadIdx.x;
+  const int nb = K >> 4;
+  const int pairs = 16 * ((((nb + 15) >> 4) + 1) >> 1);  // 16 G2: offset of lane y's block
+  const int ba = t, bb = t + pairs;
+  const bool act_a = t < pairs && ba < nb, act_b = bb < nb;  // warp rounding leaves threads >= pairs idle
+  const int ctiles = K >> 6;
+  const int lane = t & 31, warp = t >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  float gs_tensor = 0.0f;
+  if (!ROW_SCALE) gs_tensor = __fdiv_rn(__ldg(amax_in), 2688.0f);
+  float2* g = xch + (t >> 4) * 256;  // this half-warp's group pair
+  const int r = t & 15;
+
+  if (t == 0) {
+    for (int b = 0; b < NST; ++b) mbar_init(&bar[b], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  uint32_t pending = 0, pending_parity = 0;
+  if (t == 0) {
+    for (int b = 0; b < NST; ++b) {
+      const int64_t rb = blockIdx.x + static_cast<int64_t>(b) * gridDim.x;
+      if (rb < rows) {
+        mbar_arrive_expect_tx(&bar[b], row_bytes);
+        bulk_load(stages + b * static_cast<size_t>(row_bytes), src + rb * row_bytes, row_bytes, &bar[b]);
+        pending |= 1u << b;
+      }
+    }
+  }
+  int it = 0;
+  for (int64_t row = blockIdx.x; row < rows_pad; row += gridDim.x, ++it) {
+    if (row >= rows) {
+      if (act_a) sf[blocked_offset(row, ba, ctiles)] = 0;
+      if (act_b) sf[blocked_offset(row, bb, ctiles)] = 0;
+      continue;
+    }
+    const int b = it % NST;
+    const bool ok = mbar_wait(&bar[b], static_cast<uint32_t>(it / NST) & 1u, kErrWaitTimeoutProducer);
+    if (ok && t == 0) pending &= ~(1u << b);
+    if (__syncthreads_or(!ok)) break;  // a staged row never arrived: stop (error recorded)
+    const unsigned char* stage = stages + b * static_cast<size_t>(row_bytes);
+    float2 v[16];
+    {
+      float fa[16], fb[16];
+      if (act_a) {
+        unpack16<DT>(smem_raw16<DT>(stage, ba), fa);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) fa[i] = 0.0f;
+      }
+      if (act_b) {
+        unpack16<DT>(smem_raw16<DT>(stage, bb), fb);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) fb[i] = 0.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = make_float2(fa[i], fb[i]);
+    }
+    if (ROT) {  // K % 256 == 0: act_a and act_b are uniform over each half-warp
+      bfly16x2(v);  // digits 0, 1 (within the chunk)
+      if (act_a) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 2)
+          *reinterpret_cast<float4*>(g + xpos2(r, i)) = make_float4(v[i].x, v[i].y, v[i + 1].x, v[i + 1].y);
+      }
+      __syncwarp();
+      if (act_a) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = g[xpos2(i, r)];
+      }
+      bfly16x2(v);  // digits 2, 3 (across the groups' chunks): output 16 i + r in v[i]
+      __syncwarp();
+      if (act_a) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) g[xpos2(i, r)] = v[i];
+      }
+      __syncwarp();
+      if (act_a) {  // back to 16 consecutive outputs per thread: the NVFP4 block
+        const float2 s16 = make_float2(0.0625f, 0.0625f);
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const float4 w = *reinterpret_cast<const float4*>(g + xpos2(r, i));
+          v[i] = mul2(make_float2(w.x, w.y), s16);
+          v[i + 1] = mul2(make_float2(w.z, w.w), s16);
+        }
+      }
+      __syncwarp();
+    }
+    float bma = 0.0f, bmb = 0.0f;  // block maxima (inactive lanes hold zeros)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      bma = fmaxf(bma, fabsf(v[i].x));
+      bmb = fmaxf(bmb, fabsf(v[i].y));
+    }
+    float gs = gs_tensor;
+    if (ROW_SCALE) {
+      const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(fmaxf(bma, bmb)));
+      if (lane == 0) red[it & 1][warp] = __uint_as_float(wm);
+      __syncthreads();
+      const float rm = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < nw ? __float_as_uint(red[it & 1][lane]) : 0u));
+      gs = __fdiv_rn(rm, 2688.0f);
+      if (t == 0) row_scale[row] = gs;
+    } else {
+      __syncthreads();
+    }
+    // every thread has read this row's stage: refill it with the row NST iterations ahead
+    if (t == 0) {
+      const int64_t rn = row + static_cast<int64_t>(NST) * gridDim.x;
+      if (rn < rows) {
+        mbar_arrive_expect_tx(&bar[b], row_bytes);
+        bulk_load(stages + b * static_cast<size_t>(row_bytes), src + rn * row_bytes, row_bytes, &bar[b]);
+        pending |= 1u << b;
+        pending_parity = (pending_parity & ~(1u << b)) | (((static_cast<uint32_t>(it / NST) + 1u) & 1u) << b);
+      }
+    }
+    if (act_a) {
+      const BlockScale sa = block_scale(bma, gs), sb = block_scale(bmb, gs);
+      uint2 pa, pb;
+      block_codes2(v, sa, sb, pa, pb);
+      *reinterpret_cast<uint2*>(q + row * (K >> 1) + 8 * ba) = pa;
+      sf[blocked_offset(row, ba, ctiles)] = static_cast<uint8_t>(sa.sfb);
+      if (act_b) {
+        *reinterpret_cast<uint2*>(q + row * (K >> 1) + 8 * bb) = pb;
+        sf[blocked_offset(row, bb, ctiles)] = static_cast<uint8_t>(sb.sfb);
+      }
+    }
+  }
+  if (t == 0) {
+    for (int b = 0; b < NST; ++b)
+      if (pending & (1u << b)) mbar_wait(&bar[b], (pending_parity >> b) & 1u, kErrWaitTimeoutDrain);
+  }
+}
+
 // Per-tensor absmax of n elements (n % 8 == 0 for 16-bit types, % 4 for fp32) into *out
 // (as the bits of a non-negative float, combined with atomicMax; *out must start at 0).
 template <int DT>
@@ -452,14 +685,26 @@ static int sm_count() {
 template <int DT, bool ROT, bool ROW_SCALE>
 static cudaError_t launch_quant_t(const void* x, int64_t rows, int64_t rows_pad, int K, const float* amax_in,
                                   uint8_t* q, uint8_t* sf, float* row_scale, cudaStream_t st) {
-  const int threads = ((K >> 4) + 31) / 32 * 32;
+  // rotated rows of up to 8192 elements: two blocks per thread (nvfp4_quant_pair_kernel)
+  bool pair = false;
+  void (*fn)(const void*, int64_t, int64_t, int, const float*, uint8_t*, uint8_t*, float*, int) =
+      nvfp4_quant_kernel<DT, ROT, ROW_SCALE>;
+  if constexpr (ROT) {
+    if (K <= 8192) {
+      pair = true;
+      fn = nvfp4_quant_pair_kernel<DT, ROT, ROW_SCALE>;
+    }
+  }
+  const int pairs = 16 * ((((K >> 4) + 15) / 16 + 1) / 2);  // threads owning a block pair
+  const int threads = pair ? (pairs + 31) / 32 * 32 : ((K >> 4) + 31) / 32 * 32;
+  const size_t xch = pair ? static_cast<size_t>(threads / 16) * 256 * sizeof(float2)
+                          : static_cast<size_t>(threads / 16) * 272 * sizeof(float);
   const size_t row_bytes = static_cast<size_t>(K) * (DT == kF32 ? 4 : 2);
-  const size_t fixed = 32 + (ROT ? static_cast<size_t>(threads / 16) * 272 * sizeof(float) : 0);
+  const size_t fixed = 32 + (ROT ? xch : 0);
   constexpr size_t kMaxSmem = 232448 - 256;  // opt-in maximum minus the static reduction buffer
   const int nst = static_cast<int>(std::min<size_t>(kQuantMaxStages, (kMaxSmem - fixed) / row_bytes));
   if (nst < 1) return cudaErrorInvalidValue;
   const size_t smem = fixed + static_cast<size_t>(nst) * row_bytes;
-  auto fn = nvfp4_quant_kernel<DT, ROT, ROW_SCALE>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
