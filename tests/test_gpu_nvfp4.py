@@ -137,6 +137,7 @@ def _operands(m, n, k, seed):
     (1, 128, 64),         # one row, one 64-wide K step
     (129, 256, 320),      # K not a multiple of 256 (last k-block has one MMA)
     (512, 768, 13824),    # FFN down-proj K
+    (700, 640, 2048),     # several CTA-pair tiles, the last pair's second CTA partly past M
 ])
 def test_gemm_accumulators_and_epilogue_vs_fp64(cuda, m, n, k):
     from slimdit import ops
