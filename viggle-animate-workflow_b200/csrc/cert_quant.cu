@@ -30,7 +30,7 @@
 // 2. Row maximum. A = max(|S'| - D) <= max |S_ref| (rounded down), A0 = max |S'| over exact
 //    groups, B = max(|S'| + D) over the other groups (rounded up). B < A means the maximum is
 //    exact (A0). Otherwise only outputs with |S'| + D >= A can hold it: their chains are run
-//    (about one per row) and a second block barrier combines them with A0.
+//    (about one per row) by the row's fixer warp, which combines them with A0.
 // 3. Codes. With r16 = fl(1 / (16 scale)), rint(S' r16) equals the reference's code unless
 //    S' r16 lies within 2^-13 + D r16 of a half-integer (2^-13 covers the reciprocal and the
 //    reference's division rounding). Such outputs of exact groups take the IEEE division.
@@ -40,7 +40,8 @@
 // when it is the same for every scale in it) and lists the candidates for the maximum; outputs
 // whose code is not certain are listed too. The fixer runs the listed chains from the staged
 // row in shared memory, one output per lane, settles the scale and overwrites the provisional
-// codes, then reuses the row's buffer.
+// codes, then restages the row's buffer (three buffers where shared memory allows, so the
+// streamers run up to two rows ahead of the fixers).
 // A chain evaluates chunks 0..c0-1 in four independent partial sums (exact in any order) and
 // only chunks c0..15 as the reference's sequential chain.
 //
