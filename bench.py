@@ -504,9 +504,14 @@ def run_secondary(torch, dev, lib, world: int, rank: int, steps: int, barrier, r
     ffn_ops = 2.0 * FFN_TOKENS * 28672 * 5376 + 2.0 * FFN_TOKENS * 5376 * 14336
     res["ffn_swiglu"] = {"M": mm, "fc1": [28672, 5376], "fc2": [5376, 14336], "ms": round(ms, 4),
                          "TOPS": round(ffn_ops / (ms * 1e-3) / 1e12, 1)}
+    # the layer's linears together: their ops over the sum of their times
+    layer_ops = 2.0 * FFN_TOKENS * (21504 * 5376 + 5376 * 7168) + ffn_ops
+    layer_ms = sum(v["ms"] for v in res.values())
     out["minimax_h3"] = {"workload": f"MiniMax-H3 linears at {FFN_TOKENS} tokens (split over the ranks): qkv, "
                                      "out_proj, and the FFN fc1 -> fused SwiGLU -> rotate+requant -> fc2",
-                         "shapes": res, "unit": "TOPS", "scaling": "strong", "steps": steps}
+                         "shapes": res, "ms_per_step": round(layer_ms, 4),
+                         "value": round(layer_ops / (layer_ms * 1e-3) / 1e12, 1), "unit": "TOPS",
+                         "scaling": "strong", "steps": steps}
     del xh, xo, q1, s1, q2, s2
     torch.cuda.empty_cache()
 
@@ -1014,7 +1019,9 @@ def run_ours(args) -> int:
             peak_hbm = float(peaks.get("hbm_gbs", 6650.0))
             for key in ("convert_reference_order", "convert_butterfly_order", "convert_nvfp4"):
                 secondary[key]["frac_of_measured_hbm"] = round(secondary[key]["value"] / (world * peak_hbm), 4)
-            secondary["ffn_pair"]["frac_of_i8_peak"] = round(secondary["ffn_pair"]["value"] / (world * peak), 4)
+            for key in ("ffn_pair", "minimax_h3"):
+                if "value" in secondary.get(key, {}):
+                    secondary[key]["frac_of_i8_peak"] = round(secondary[key]["value"] / (world * peak), 4)
             # dense FP4 (kind::mxf4nvf4) issues at four times kind::f16's rate
             fp4_peak = 2.0 * peak
             nv = secondary["nvfp4_up_proj"]
