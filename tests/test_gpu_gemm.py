@@ -388,3 +388,67 @@ def test_ffn_config2_slice_stage_by_stage(cuda):
     # stage 4: the output against the GPU's own hidden codes
     acc2 = oracle.int8_gemm_i32(hq_n, qd)
     check_bf16_within_one_ulp(out, oracle.linear_reference_f64(acc2, sho.reshape(-1), sd.reshape(-1), None), "ffn out")
+
+
+def test_minimax_swiglu_ffn_slice_stage_by_stage(cuda):
+    """The MiniMax-H3 FFN at its real widths (5376 -> 2 x 14336 with the fused SwiGLU -> 5376,
+    tools/bench_int8.py:23-28, slimdit/mapping.py:99-101) on 1024 tokens, through the C entry
+    slim_ffn_i8 with the test's own workspaces, stage by stage:
+    * activation codes/scales = the reference-order quantisation of x (bit-exact);
+    * hidden h: within 2 bf16 ulp of bf16(up * bf16(silu(gate))) evaluated in fp64 from the
+      epilogue's bf16 up and gate (fp32 pre-activation chain restated exactly; one ulp for a
+      flip of the rounded silu, one for the final rounding), at most 1 in 10^3 beyond half an ulp;
+    * hidden codes/scales = the reference-order quantisation of the GPU's own h (bit-exact);
+    * output within 1 bf16 ulp of the fp64 dequant of those codes."""
+    from slimdit import _native, ops
+    from slimdit.int8 import quantize_convrot_weight
+    m, k, f = 1024, 5376, 14336
+    x = synthetic.activations(m, k, seed=61)
+    q1, s1 = quantize_convrot_weight(synthetic.weight(2 * f, k, seed=62))  # rows [up; gate]
+    q2, s2 = quantize_convrot_weight(synthetic.weight(k, f, seed=63))
+    b1 = synthetic.bf16_round_f32(np.random.default_rng(64).standard_normal(2 * f).astype(np.float32) * 0.02)
+    dev = cuda
+    q1i, s1i, b1i = ops.swiglu_interleave(torch.from_numpy(q1).to(dev), torch.from_numpy(s1.reshape(-1)).to(dev),
+                                          torch.from_numpy(b1).to(dev).to(torch.bfloat16))
+    q2d, s2d = torch.from_numpy(q2).to(dev), torch.from_numpy(s2.reshape(-1)).to(dev)
+    xt = torch.from_numpy(x).to(dev).to(torch.bfloat16)
+    xq = torch.empty((m, k), dtype=torch.int8, device=dev)
+    sx = torch.empty((m,), dtype=torch.float32, device=dev)
+    h = torch.empty((m, f), dtype=torch.bfloat16, device=dev)
+    hq = torch.empty((m, f), dtype=torch.int8, device=dev)
+    sh = torch.empty((m,), dtype=torch.float32, device=dev)
+    out = torch.empty((m, k), dtype=torch.bfloat16, device=dev)
+    lib = _native.load()
+    _native.check(lib.slim_ffn_i8(xt.data_ptr(), _native.BF16, q1i.data_ptr(), s1i.data_ptr(), b1i.data_ptr(),
+                                  q2d.data_ptr(), s2d.data_ptr(), None, out.data_ptr(), xq.data_ptr(), sx.data_ptr(),
+                                  h.data_ptr(), hq.data_ptr(), sh.data_ptr(), m, k, f, _native.EPI_SWIGLU, None))
+    torch.cuda.synchronize()
+    # stage 1: activation codes
+    qx, sxo = oracle.quantize_activations(x)
+    assert np.array_equal(xq.cpu().numpy(), qx)
+    assert np.array_equal(sx.cpu().numpy().view(np.uint32), sxo.reshape(-1).view(np.uint32))
+    # stage 2: the hidden activation from the epilogue's bf16 up and gate,
+    # bf16(fma(float(acc), sa * sb, bias)) with the fp32 scale product
+    acc1 = oracle.int8_gemm_i32(qx, q1)
+
+    def lin(cols):
+        sp = (sxo.reshape(-1, 1).astype(np.float32) * s1.reshape(-1)[cols].reshape(1, -1)).astype(np.float32)
+        v = acc1[:, cols].astype(np.float32).astype(np.float64) * sp.astype(np.float64) + b1[cols].astype(np.float64)
+        return oracle.bf16_round(v.astype(np.float32)).astype(np.float64)
+
+    up, gate = lin(slice(0, f)), lin(slice(f, 2 * f))
+    silu = oracle.bf16_round((gate / (1.0 + np.exp(-gate))).astype(np.float32)).astype(np.float64)
+    ref = up * silu
+    hv = h.cpu().float().numpy().astype(np.float64)
+    ulp = oracle.bf16_ulp(ref)
+    err = np.abs(hv - ref)
+    assert np.all(err <= 2 * ulp), float((err / ulp).max())
+    assert (err > 0.5 * ulp * (1 + 2.0**-5)).mean() <= 1e-3
+    # stage 3: hidden codes of the GPU's own h
+    qh, sho = oracle.quantize_activations(h.cpu().float().numpy())
+    hq_n = hq.cpu().numpy()
+    assert np.array_equal(hq_n, qh)
+    assert np.array_equal(sh.cpu().numpy().view(np.uint32), sho.reshape(-1).view(np.uint32))
+    # stage 4: the output against the GPU's own hidden codes
+    acc2 = oracle.int8_gemm_i32(hq_n, q2)
+    check_bf16_within_one_ulp(out, oracle.linear_reference_f64(acc2, sho.reshape(-1), s2.reshape(-1), None), "swiglu out")
