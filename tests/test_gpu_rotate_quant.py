@@ -285,8 +285,8 @@ def _stress_rows(k: int, dtype) -> np.ndarray:
     return np.stack(rows).astype(np.float32)
 
 
-@pytest.mark.parametrize("k", [1280, 2816, 5120, 13824, 16384])
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("k", [1280, 2816, 5120, 7168, 10240, 10496, 13824, 16384])  # 10240 / 10496: either side of
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])     # the narrow/wide switch
 def test_certified_reference_order_stress_vs_oracle(cuda, k, dtype):
     from slimdit import ops
     xt = torch.from_numpy(_stress_rows(k, dtype)).to(cuda).to(dtype)
