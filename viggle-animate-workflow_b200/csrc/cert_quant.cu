@@ -686,8 +686,9 @@ __global__ void __maxnreg__(MAXR) cert_rotate_quant_kernel(const void* __restric
 // K = 13824 keep two CTAs per SM. Measured on B200 (bit-identical outputs), the narrow
 // configuration against the wide one: 0.646 vs 0.803 ms at 65536 x 6400, 0.655 vs 0.811 at
 // x 7168, 0.827 vs 0.878 at x 8192, 0.438 vs 0.510 at 32768 x 9216, 0.505 vs 0.547 at x 10240;
-// from 48 groups on it holds one CTA per SM and loses (0.768 vs 0.610 at x 12288, 1.09 vs 0.74
-// on the FFN hidden at x 13824). Three staged rows where they fit in a CTA's shared memory without fewer CTAs per SM
+// at 44 groups it depends on the input (0.544 vs 0.576 ms on activations, 0.647 vs 0.623 on a
+// GELU hidden); from 48 groups on it holds one CTA per SM and loses (0.768 vs 0.610 at x 12288,
+// 1.09 vs 0.74 on the FFN hidden at x 13824). Three staged rows where they fit in a CTA's shared memory without fewer CTAs per SM
 // than two would give, else two: measured on B200 (bit-identical outputs), 32768 x 5120 bf16
 // activations 0.269 -> 0.266 ms and the FFN hidden 115200 x 13824 2.91 -> 2.73 ms with three;
 // four rows, or the half transpose on narrow rows (+11 % time), were slower.
