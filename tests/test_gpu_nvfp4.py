@@ -91,8 +91,9 @@ def test_pack_codes_at_rounding_ties(cuda):
     (200, 256, True, torch.float16),
     (40, 16384, True, torch.float32),      # widest row: fewer rows staged in shared memory
     (130, 1280, True, torch.bfloat16),     # two blocks per thread, odd group count (idle y lanes)
-    (33, 7936, True, torch.float16),       # 31 groups, just below the two-block kernel's limit
-    (65, 8192, True, torch.float32),       # at the limit, fp32 rows
+    (33, 7936, True, torch.float16),       # 31 groups, two blocks per thread
+    (65, 8192, True, torch.float32),       # fp32 rows: the one-block-per-thread kernel
+    (50, 10240, True, torch.bfloat16),     # the two-block kernel's widest rows
 ])
 def test_activation_quant_bit_exact_vs_oracle(cuda, m, k, rotate, dtype):
     from slimdit import ops

@@ -423,10 +423,12 @@ __global__ void __launch_bounds__(1024) nvfp4_quant_kernel(const void* __restric
 // shared memory by bulk copies, nst (1..3, as many as shared memory holds) rows ahead: the HBM
 // reads of the next rows overlap this row's arithmetic without holding registers. Rows in
 // [rows, rows_pad) only get zero scale bytes (padding of the last 128-row tile).
-// ROW_SCALE as in nvfp4_quant_kernel. Rotated rows of up to 8192 elements take this kernel: measured
-// against nvfp4_quant_kernel (bit-identical outputs), 115200 x 5120 rotated bf16 0.696 -> 0.577 ms;
-// at K = 13824 (one CTA of 14 warps per SM at 95 registers) and without the rotation the
-// one-block-per-thread kernel is faster (0.296 vs 0.310 ms; 0.151 vs 0.170 ms).
+// ROW_SCALE as in nvfp4_quant_kernel. Rotated 16-bit rows of up to 10240 elements take this kernel,
+// which keeps two CTAs per SM there at 95 registers. Measured against nvfp4_quant_kernel
+// (bit-identical outputs): rotated bf16 115200 x 5120 0.696 -> 0.577 ms, 32768 x 10240
+// 0.468 -> 0.364 ms, equal at 6144-8192. From 11264 on it holds one CTA per SM and is slower
+// (0.523 vs 0.512 ms at 11264, 0.610 vs 0.585 at 13824). It is also slower without the rotation
+// (0.170 vs 0.151 ms) and on fp32 rows (0.157 vs 0.151 ms at 10240).
 template <int DT, bool ROT, bool ROW_SCALE>
 __global__ void __launch_bounds__(512) nvfp4_quant_pair_kernel(const void* __restrict__ x, int64_t rows,
                                                            int64_t rows_pad, int K,
@@ -685,12 +687,12 @@ static int sm_count() {
 template <int DT, bool ROT, bool ROW_SCALE>
 static cudaError_t launch_quant_t(const void* x, int64_t rows, int64_t rows_pad, int K, const float* amax_in,
                                   uint8_t* q, uint8_t* sf, float* row_scale, cudaStream_t st) {
-  // rotated rows of up to 8192 elements: two blocks per thread (nvfp4_quant_pair_kernel)
+  // rotated 16-bit rows of up to 10240 elements: two blocks per thread (nvfp4_quant_pair_kernel)
   bool pair = false;
   void (*fn)(const void*, int64_t, int64_t, int, const float*, uint8_t*, uint8_t*, float*, int) =
       nvfp4_quant_kernel<DT, ROT, ROW_SCALE>;
-  if constexpr (ROT) {
-    if (K <= 8192) {
+  if constexpr (ROT && DT != kF32) {
+    if (K <= 10240) {
       pair = true;
       fn = nvfp4_quant_pair_kernel<DT, ROT, ROW_SCALE>;
     }
